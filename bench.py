@@ -1,0 +1,463 @@
+"""Benchmark of the W8A16 quantized linear layer on B200 (BASELINE.json metric).
+
+Default workload: the full Qwen3-0.6B decode-step
+projection set -- 28 layers x {fused QKV 4096x1024, o 1024x2048, fused gate_up
+6144x1024, down 1024x3072} + lm_head 151936x1024 = 113 GEMMs, int8 weights with
+per-row bf16 scales (~0.6 GB streamed per pass) -- at batch M in {1, 8, 32, 64}.
+One step = one pass at every M (4 x 113 launches), replayed from CUDA graphs
+whose kernels are chained with programmatic dependent launch.  Weights: random
+N(0, 0.02), seeded, quantised on the GPU; activations N(0, 1) bf16, seeded per
+rank (synthetic data -- no checkpoints).
+
+``value``   algorithmic HBM bytes (int8 weights + bf16 scales + bf16 x + bf16 y)
+            of all ranks / device time of the step (max over ranks), GB/s.
+``e2e``     the same metric through the public API with host buffers: each step
+            copies every GEMM input from pinned host memory and reads the
+            lm_head logits back, inside the timed region.
+Other workloads (``--workload``): prefill (config 2, TFLOP/s), w4a16 (config 3),
+llama (config 4; ``--lm-head-shard`` vocab-shards the lm_head with an NCCL
+all-gather).
+
+``--impl reference`` times the reference's CPU path (dequantise-then-matmul,
+restated in ``oracle/``) on the host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+QWEN_LAYER = [("qkv", 4096, 1024), ("o", 1024, 2048), ("gate_up", 6144, 1024), ("down", 1024, 3072)]
+QWEN_HEAD = ("lm_head", 151936, 1024)
+LLAMA_LAYER = [("qkv", 5120, 3072), ("o", 3072, 3072), ("gate_up", 16384, 3072), ("down", 3072, 8192)]
+LLAMA_HEAD = ("lm_head", 128256, 3072)
+LAYERS = 28
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profiled_traffic(kernel_key: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get(kernel_key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU paths
+def cpu_path_sample(workload_shapes, m, budget_s=10.0, seed=0):
+    """The reference's CPU path (dequantise, fp32 matmul, bf16 cast -- restated in
+    ``oracle/``) over a bounded sample of the workload's GEMMs.  Returns
+    (GB/s of algorithmic bytes, seconds, description, threads)."""
+    import numpy as np
+    from threadpoolctl import threadpool_info
+
+    from oracle import quant_oracle as O
+    rng = np.random.default_rng(seed)
+    done_bytes, t_total, names = 0, 0.0, []
+    prepared = []
+    for name, n, k in workload_shapes:
+        rows = min(n, 8192)            # bounded sample of rows per GEMM
+        w = (rng.standard_normal((rows, k), dtype=np.float32) * 0.02)
+        q, s = O.quantize_int8_rowwise(w)
+        x = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
+        prepared.append((name, rows, k, q, s, x))
+    start = time.perf_counter()
+    while time.perf_counter() - start < budget_s:
+        for name, rows, k, q, s, x in prepared:
+            t0 = time.perf_counter()
+            O.linear(x, O.dequantize_int8_rowwise(q, s))
+            t_total += time.perf_counter() - t0
+            done_bytes += rows * k + 2 * rows + 2 * m * k + 2 * m * rows
+            names.append(name)
+            if time.perf_counter() - start >= budget_s:
+                break
+    threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    desc = (f"M={m}: {len(names)} GEMM calls over row samples (<=8192 rows) of "
+            f"{', '.join(sorted(set(names)))}; dequantise + numpy/BLAS fp32 matmul + bf16 cast")
+    return done_bytes / t_total / 1e9, t_total, desc, threads
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    shapes = QWEN_LAYER + [QWEN_HEAD] if args.workload != "llama" else LLAMA_LAYER + [LLAMA_HEAD]
+    per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, desc, threads = cpu_path_sample(shapes, 1, budget_s=per_step, seed=i)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per_step * 1000, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "reference CPU path (dequantise + fp32 matmul) on a bounded sample, M=1",
+                       "gpus_used": 0},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "W8A16 GEMM HBM GB/s (decode M<=64) and TFLOP/s (prefill), Qwen3-0.6B shapes"
+
+
+# ------------------------------------------------------------------ GPU paths
+def init_dist(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return world, rank, local, pg
+
+
+def build_weights(kl, shapes, layers, device, seed=1234):
+    import torch
+    gen = torch.Generator(device=device)
+    weights = []
+    for li in range(layers):
+        for j, (name, n, k) in enumerate(shapes):
+            gen.manual_seed(seed + li * 16 + j)
+            w = torch.randn(n, k, device=device, generator=gen) * 0.02
+            weights.append((f"{name}{li}", kl.quantize_int8_rowwise(w)))
+            del w
+    return weights
+
+
+def bench_decode(args, kl, world, rank, local, dist):
+    import torch
+    device = torch.device("cuda", local)
+    layer, head = (LLAMA_LAYER, LLAMA_HEAD) if args.workload == "llama" else (QWEN_LAYER, QWEN_HEAD)
+    ms_list = [int(v) for v in args.batch.split(",")] if args.batch else ([1, 64, 256] if args.workload == "llama" else [1, 8, 32, 64])
+    weights = build_weights(kl, layer, LAYERS, device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4321)
+    hw = torch.randn(head[1], head[2], device=device, generator=gen) * 0.02
+    weights.append(("lm_head", kl.quantize_int8_rowwise(hw)))
+    del hw
+    torch.cuda.empty_cache()
+    shard = None
+
+    xg = torch.Generator(device=device)
+    xg.manual_seed(99 + rank)
+    passes = {}
+    for m in ms_list:
+        items = []
+        for name, p in weights:
+            n, k = p.data.shape
+            x = torch.randn(m, k, device=device, generator=xg).to(torch.bfloat16)
+            y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            items.append((name, p, x, y))
+        passes[m] = items
+
+    def run_pass(m):
+        for name, p, x, y in passes[m]:
+            kl.quant_linear(x, p, out=y, pdl=True)
+
+    # algorithmic bytes of one pass at each M
+    def pass_bytes(m):
+        b = 0
+        for name, p, x, y in passes[m]:
+            n, k = p.data.shape
+            b += n * k + 2 * n + 2 * m * k + 2 * m * n
+        return b
+
+    launches_per_pass = {m: len(passes[m]) for m in ms_list}
+    for m in ms_list:                 # eager warm-up (allocates the workspace before capture)
+        run_pass(m)
+    torch.cuda.synchronize()
+    graphs = {}
+    for m in ms_list:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_pass(m)
+        graphs[m] = g
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        for m in ms_list:
+            graphs[m].replay()
+    barrier()
+    ev = {m: [] for m in ms_list}
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            for m in ms_list:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graphs[m].replay()
+                e1.record()
+                ev[m].append((e0, e1))
+        stop.record()
+        barrier()
+    total_ms = start.elapsed_time(stop)
+    per_m_ms = {m: sum(a.elapsed_time(b) for a, b in ev[m]) / args.steps for m in ms_list}
+    ms_step = total_ms / args.steps
+    if dist is not None:
+        t = torch.tensor([ms_step], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = t.item()
+    step_bytes = sum(pass_bytes(m) for m in ms_list)
+    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+
+    # ---- e2e through the public API with host buffers
+    pinned = {m: [torch.empty(x.shape, dtype=x.dtype, pin_memory=True).copy_(x) for _, _, x, _ in passes[m]]
+              for m in ms_list}
+    head_out = {m: torch.empty(passes[m][-1][3].shape, dtype=torch.bfloat16, pin_memory=True) for m in ms_list}
+    h2d = sum(t.numel() * 2 for m in ms_list for t in pinned[m])
+    d2h = sum(t.numel() * 2 for t in head_out.values())
+
+    def e2e_step():
+        for m in ms_list:
+            for (name, p, x, y), hx in zip(passes[m], pinned[m]):
+                x.copy_(hx, non_blocking=True)
+            graphs[m].replay()
+            head_out[m].copy_(passes[m][-1][3], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        e2e_step()
+    t2.record()
+    barrier()
+    e2e_ms = s2.elapsed_time(t2) / args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
+
+    # ---- dominant kernel alone: the lm_head launch (largest single GEMM), L2-cold
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    name, p, x, y = passes[ms_list[0]][-1]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    times = []
+    for i in range(8):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        kl.quant_linear(x, p, out=y)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            times.append(a.elapsed_time(b))
+    n, k = p.data.shape
+    m0 = ms_list[0]
+    head_bytes = n * k + 2 * n + 2 * m0 * k + 2 * m0 * n
+    head_ms = statistics.median(times)
+    head_gbs = head_bytes / (head_ms * 1e-3) / 1e9
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": ("llama-3.2-3b" if args.workload == "llama" else "qwen3-0.6b") +
+                               " decode projection set (BASELINE config " + ("4" if args.workload == "llama" else "1") + ")",
+                   "batch_m": ms_list, "gemms_per_pass": launches_per_pass[ms_list[0]],
+                   "bytes_per_step": step_bytes, "weights": "int8 per-row bf16 scale, N(0,0.02) seeded",
+                   "l2": "inputs larger than L2: each pass streams >=0.6 GB of weights, no flush needed",
+                   "parallelism": f"replicas x{world}" + (" + vocab-sharded lm_head (NCCL all-gather)" if shard else ""),
+                   "launch": "CUDA graph per M, kernels chained with programmatic dependent launch"},
+        "per_m": {str(m): {"ms": round(per_m_ms[m], 4), "GB/s": round(pass_bytes(m) / (per_m_ms[m] * 1e-3) / 1e9, 1),
+                           "frac_hbm": round(pass_bytes(m) / (per_m_ms[m] * 1e-3) / 1e9 / hbm, 3)}
+                  for m in ms_list},
+        "roofline": {"bound": "hbm", "kernel": "tc_qgemm_kernel (every launch of the step)",
+                     "achieved": round(step_bytes / (ms_step * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4), "peak_source": peak_kind,
+                     "traffic": profiled_traffic(f"{args.workload}_step"),
+                     "lm_head_alone": {"ms": round(head_ms, 4), "GB/s": round(head_gbs, 1),
+                                       "frac": round(head_gbs / hbm, 3), "m": m0}},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": sum(launches_per_pass.values()) * args.steps,
+        "clocks": clocks.summary(),
+    }
+    return result
+
+
+def bench_prefill(args, kl, world, rank, local, dist):
+    import torch
+    device = torch.device("cuda", local)
+    ms_list = [int(v) for v in args.batch.split(",")] if args.batch else [512, 2048, 8192]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(77)
+    weights = []
+    for name, n, k in QWEN_LAYER:
+        w = torch.randn(n, k, device=device, generator=gen) * 0.02
+        weights.append((name, kl.quantize_int8_rowwise(w), name == "gate_up" and args.swiglu))
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    res = {}
+    total_flops, total_ms = 0.0, 0.0
+    with ClockSampler(local) as clocks:
+        for m in ms_list:
+            items = []
+            for name, p, sw in weights:
+                n, k = p.data.shape
+                x = torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16)
+                y = torch.empty(m, n // 2 if sw else n, device=device, dtype=torch.bfloat16)
+                items.append((name, p, sw, x, y))
+            for _ in range(args.warmup):
+                for name, p, sw, x, y in items:
+                    kl.quant_linear(x, p, out=y, swiglu=sw)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                for name, p, sw, x, y in items:
+                    kl.quant_linear(x, p, out=y, swiglu=sw, pdl=True)
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / args.steps
+            flops = sum(2 * m * p.data.shape[0] * p.data.shape[1] for _, p, _, _, _ in items)
+            res[str(m)] = {"ms": round(ms, 4), "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 1),
+                           "frac": round(flops / (ms * 1e-3) / 1e12 / tf_burst, 3)}
+            total_flops += flops
+            total_ms += ms
+    value = world * total_flops / (total_ms * 1e-3) / 1e12
+    return {"metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-0.6b prefill layer GEMMs (BASELINE config 2)", "batch_m": ms_list,
+                       "swiglu": bool(args.swiglu), "l2": "activations+weights per M exceed L2 at M>=2048"},
+            "per_m": res,
+            "roofline": {"bound": "tensor", "achieved": round(value / world, 1), "peak": tf_burst, "unit": "TFLOP/s",
+                         "frac": round(value / world / tf_burst, 4), "peak_source": peak_kind, "traffic": None},
+            "gpu_launches": len(weights) * len(ms_list) * (args.steps + args.warmup),
+            "clocks": clocks.summary()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode")
+    ap.add_argument("--batch", default="", help="comma-separated M values (overrides the workload's)")
+    ap.add_argument("--swiglu", action="store_true", help="prefill: fuse SwiGLU into gate_up")
+    ap.add_argument("--lm-head-shard", action="store_true", help="llama: vocab-shard the lm_head + NCCL all-gather")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    kl = importlib.import_module("gpu-kernel-lab_b200")
+    world, rank, local, dist = init_dist(args)
+    try:
+        if args.workload == "prefill":
+            result = bench_prefill(args, kl, world, rank, local, dist)
+        else:
+            result = bench_decode(args, kl, world, rank, local, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "prefill":
+            shapes = QWEN_LAYER + [QWEN_HEAD] if args.workload != "llama" else LLAMA_LAYER + [LLAMA_HEAD]
+            v, secs, desc, threads = cpu_path_sample(shapes, 1, budget_s=10.0)
+            result["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                                      "sample": desc + f" ({secs:.1f} s)"}
+        elif rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = None
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,29 @@
+"""B200-native (sm_100a) weight-only quantized linear layer (W8A16 / W4A16).
+
+A drop-in for the quantized-Linear path of yashlabs-trying/gpu-kernel-lab:
+the reference's Python interfaces (``project``, ``quantize_int8``,
+``dequantize_int8``, ``CalibratedInt8``, ``PackedInt4``, ``quantize_int4``,
+``dequantize_int4``, ``int4_gemv``, ``int4_lm_head_topk``, the
+``serving/kernel_policy.py`` dispatch contract) backed by hand-written CUDA
+kernels in ``libkl_b200.so`` (C ABI: ``include/kl_b200.h``).
+
+The directory name contains hyphens, so import it with
+``importlib.import_module("gpu-kernel-lab_b200")``.
+"""
+from . import _native
+from .activation_int8 import (CalibratedInt8, RowwiseInt8, dequantize_int8, dequantize_int8_rowwise,
+                              quantize_int8, quantize_int8_rowwise)
+from .cuda_decode import extension, project
+from .kernels import int4_gemv, int4_lm_head_topk
+from .linear import QuantLinear, quant_linear, weight_spec
+from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequantize_int4_asym, quantize_int4,
+                           quantize_int4_asym)
+from .native_ops import dequantize_native
+
+__all__ = [
+    "CalibratedInt8", "RowwiseInt8", "PackedInt4", "PackedInt4Asym", "QuantLinear",
+    "quantize_int8", "dequantize_int8", "quantize_int8_rowwise", "dequantize_int8_rowwise",
+    "quantize_int4", "dequantize_int4", "quantize_int4_asym", "dequantize_int4_asym",
+    "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec",
+    "dequantize_native",
+]

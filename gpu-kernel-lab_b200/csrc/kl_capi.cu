@@ -1,0 +1,400 @@
+// C-ABI entry points (include/kl_b200.h): argument validation, path choice
+// (tcgen05 GEMM vs CUDA-core GEMV), TMA descriptor encoding and launches.
+// Nothing here allocates device memory or synchronises the stream, so every
+// entry point can be captured into a CUDA graph.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "kl_common.cuh"
+#include "kl_internal.h"
+
+namespace kl {
+
+// Device status word: bounded in-kernel waits record KL_ERR_TIMEOUT here.
+__device__ int g_status_word = 0;
+
+size_t head_topk_candidate_bytes(int n, int top_k);
+cudaError_t launch_topk(const void* logits, bool xbf16, int n, int top_k, void* cand, float* values,
+                        int64_t* ids, cudaStream_t s);
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KL_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0, minor = 0;
+  int* status = nullptr;
+  bool ready = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mutex;
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(KL_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_status_word)) != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    d.status = static_cast<int*>(p);
+    d.ready = true;
+  }
+  *out = d;
+  return KL_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return fail(KL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return KL_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool is_w4(int f) { return f == KL_W4_SYM || f == KL_W4_ASYM; }
+bool is_grouped(int f) { return f == KL_W8_GROUP || is_w4(f); }
+size_t act_bytes(int dt) { return dt == KL_DT_F32 ? 4 : 2; }
+
+// Whether the tcgen05 kernel takes this problem (device capability aside).
+bool tc_shape_ok(int k, int w_format, int group) {
+  if (w_format == KL_W8_ROW) return k % 16 == 0;
+  if (is_w4(w_format)) return group == 128 && k % 128 == 0;
+  return false;
+}
+
+int validate_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
+                    const void* scales, const void* zeros, const float* inverse, int swiglu, const void* y,
+                    int flags) {
+  if (!x || !w || !y) return fail(KL_ERR_INVALID, "x, w and y must be non-null");
+  if (m <= 0 || k <= 0 || n <= 0) return fail(KL_ERR_INVALID, "dimensions must be positive (m=%d k=%d n=%d)", m, k, n);
+  if (x_dtype != KL_DT_BF16 && x_dtype != KL_DT_F16) return fail(KL_ERR_INVALID, "activations must be bf16 or f16");
+  if (w_format < KL_W8_ROW || w_format > KL_BF16_DENSE) return fail(KL_ERR_INVALID, "unknown weight format %d", w_format);
+  if (swiglu && (n % 2)) return fail(KL_ERR_INVALID, "gate/up requires two equal row sets");
+  if (is_grouped(w_format) && (group <= 0 || k % group)) return fail(KL_ERR_INVALID, "group must divide K");
+  if (is_w4(w_format) && (k % 2 || group % 2)) return fail(KL_ERR_INVALID, "4-bit weights need an even K and group");
+  if (w_format != KL_BF16_DENSE && !scales) return fail(KL_ERR_INVALID, "scales required");
+  if (w_format == KL_W8_GROUP && !inverse) return fail(KL_ERR_INVALID, "inverse channel vector required");
+  if (w_format == KL_W4_ASYM && !zeros) return fail(KL_ERR_INVALID, "zero points required");
+  if ((flags & KL_FLAG_FORCE_SIMT) && (flags & KL_FLAG_FORCE_TC)) return fail(KL_ERR_INVALID, "conflicting path flags");
+  return KL_OK;
+}
+
+}  // namespace
+}  // namespace kl
+
+using namespace kl;
+
+extern "C" {
+
+const char* kl_status_string(int status) {
+  switch (status) {
+    case KL_OK: return "ok";
+    case KL_ERR_INVALID: return "invalid argument";
+    case KL_ERR_UNSUPPORTED: return "unsupported";
+    case KL_ERR_CUDA: return "CUDA error";
+    case KL_ERR_WORKSPACE: return "workspace missing or too small";
+    case KL_ERR_TIMEOUT: return "in-kernel wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* kl_last_error(void) { return g_last_error; }
+
+int kl_version(void) { return 100; }
+
+size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, int flags) {
+  if (m <= 0 || n <= 0 || k <= 0 || (flags & KL_FLAG_FORCE_SIMT)) return 0;
+  if (!(w_format == KL_W8_ROW || is_w4(w_format))) return 0;
+  int sm = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sm = v;
+  } else {
+    cudaGetLastError();
+  }
+  const int mm = is_w4(w_format) ? std::min(m, 64) : m;
+  const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, sm);
+  return plan.ok ? plan.workspace : 0;
+}
+
+int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
+              const void* scales, const void* zeros, const float* inverse, int swiglu, void* y, void* workspace,
+              size_t workspace_bytes, int flags, void* stream) {
+  int rc = validate_linear(x, x_dtype, m, k, w, w_format, n, group, scales, zeros, inverse, swiglu, y, flags);
+  if (rc != KL_OK) return rc;
+  DeviceInfo di;
+  if ((rc = device_info(&di)) != KL_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n_out = swiglu ? n / 2 : n;
+  const bool xbf16 = x_dtype == KL_DT_BF16;
+  const bool transposed = (flags & KL_FLAG_Y_TRANSPOSED) != 0;
+  const bool sm100 = di.major == 10 && di.minor == 0;
+  const bool tc = sm100 && !(flags & KL_FLAG_FORCE_SIMT) && tc_shape_ok(k, w_format, group) && aligned16(x) &&
+                  aligned16(w);
+  if ((flags & KL_FLAG_FORCE_TC) && !tc)
+    return fail(KL_ERR_UNSUPPORTED, "tcgen05 path not applicable (format %d, K %d, group %d, sm%d%d)", w_format, k,
+                group, di.major, di.minor);
+  if (!sm100) return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
+  const size_t eb = act_bytes(x_dtype);
+
+  if (tc) {
+    const int mchunk = is_w4(w_format) ? 64 : m;
+    for (int m0 = 0; m0 < m; m0 += mchunk) {
+      const int mm = std::min(mchunk, m - m0);
+      const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, di.sm_count);
+      if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for m=%d n=%d k=%d", mm, n, k);
+      if (!workspace || workspace_bytes < plan.workspace)
+        return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
+                    workspace ? workspace_bytes : 0);
+      TcParams p;
+      std::memset(&p, 0, sizeof(p));
+      const char* xb = static_cast<const char*>(x) + static_cast<size_t>(m0) * k * eb;
+      if (is_w4(w_format)) {
+        rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k / 2, n, k / 2, 64, 64,
+                       CU_TENSOR_MAP_SWIZZLE_64B);
+      } else {
+        rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      }
+      if (rc != KL_OK) return rc;
+      rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, k, mm,
+                     static_cast<uint64_t>(k) * eb, 64, plan.n_mma, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != KL_OK) return rc;
+      p.scales = scales;
+      p.zeros = zeros;
+      p.y = static_cast<char*>(y) + (transposed ? static_cast<size_t>(m0) : static_cast<size_t>(m0) * n_out) * eb;
+      p.counters = static_cast<int*>(workspace);
+      p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+      p.m = mm;
+      p.n = n;
+      p.k = k;
+      p.n_out = n_out;
+      p.m_tiles = plan.m_tiles;
+      p.n_tiles = plan.n_tiles;
+      p.kb_total = plan.kb_total;
+      p.units = plan.units;
+      p.y_transposed = transposed ? 1 : 0;
+      p.ldy = transposed ? m : n_out;
+      p.status = di.status;
+      const cudaError_t e = launch_tc(p, plan, w_format, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
+      if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
+    }
+    return KL_OK;
+  }
+
+  const GemvPlan gp = plan_gemv(m, n_out, k, w_format, group, swiglu != 0, aligned16(w), di.sm_count);
+  GemvArgs a;
+  a.x = x;
+  a.w = w;
+  a.scales = scales;
+  a.zeros = zeros;
+  a.inverse = inverse;
+  a.y = y;
+  a.m = m;
+  a.k = k;
+  a.n_out = n_out;
+  a.group = group;
+  a.kpad = gp.kpad;
+  a.y_transposed = transposed ? 1 : 0;
+  a.ldy = transposed ? m : n_out;
+  const cudaError_t e = launch_gemv(a, gp, w_format, swiglu != 0, xbf16, s);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  return KL_OK;
+}
+
+int kl_project(const void* x, int k, const void* w, int w_is_int8, const float* scales, const float* inverse, int n,
+               int group, int warps, int persistent, int swiglu, void* y, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  (void)persistent;
+  if (!x || !w || !y) return fail(KL_ERR_INVALID, "same CUDA device required");
+  if (k <= 0 || n <= 0) return fail(KL_ERR_INVALID, "w: contiguous nonempty [N,K]");
+  if (!(warps == 1 || warps == 4 || warps == 8)) return fail(KL_ERR_INVALID, "warps must be 1,4,8");
+  if (swiglu && n % 2) return fail(KL_ERR_INVALID, "gate/up requires two equal row sets");
+  if (w_is_int8) {
+    if (group <= 0 || k % group) return fail(KL_ERR_INVALID, "group must divide K");
+    if (!scales || !inverse) return fail(KL_ERR_INVALID, "FP32 contiguous scaling buffers required");
+  }
+  return kl_linear(x, KL_DT_BF16, 1, k, w, w_is_int8 ? KL_W8_GROUP : KL_BF16_DENSE, n, group, scales, nullptr,
+                   inverse, swiglu, y, workspace, workspace_bytes, 0, stream);
+}
+
+int kl_int4_gemv(const void* x, int x_dtype, int k, const uint8_t* w, const float* scales, int n, int group,
+                 int block_n, void* y, void* stream) {
+  if (!(group == 32 || group == 64 || group == 128)) return fail(KL_ERR_INVALID, "group_size must be 32, 64, or 128");
+  if (!(block_n == 8 || block_n == 16 || block_n == 32 || block_n == 64))
+    return fail(KL_ERR_INVALID, "block_n must be 8,16,32,64");
+  // The M = 1 W4 GEMV runs on the CUDA-core kernel (no workspace).
+  return kl_linear(x, x_dtype, 1, k, w, KL_W4_SYM, n, group, scales, nullptr, nullptr, 0, y, nullptr, 0,
+                   KL_FLAG_FORCE_SIMT, stream);
+}
+
+size_t kl_int4_lm_head_topk_workspace_bytes(int n, int top_k, int block_n) {
+  (void)block_n;
+  if (n <= 0 || top_k <= 0) return 0;
+  const size_t logits = (static_cast<size_t>(n) * 2 + 255) & ~size_t(255);
+  return logits + head_topk_candidate_bytes(n, top_k);
+}
+
+int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w, const float* scales, int n, int group,
+                         int top_k, int block_n, float* values, int64_t* ids, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!values || !ids) return fail(KL_ERR_INVALID, "values and ids must be non-null");
+  if (top_k < 1 || top_k > 8 || top_k > block_n || top_k > n)
+    return fail(KL_ERR_INVALID, "top_k must be between 1 and min(8,block_n,vocabulary)");
+  const size_t need = kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n);
+  if (!workspace || workspace_bytes < need) return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+  char* logits = static_cast<char*>(workspace);
+  char* cand = logits + ((static_cast<size_t>(n) * 2 + 255) & ~size_t(255));
+  int rc = kl_int4_gemv(x, x_dtype, k, w, scales, n, group, block_n, logits, stream);
+  if (rc != KL_OK) return rc;
+  const cudaError_t e = launch_topk(logits, x_dtype == KL_DT_BF16, n, top_k, cand, values, ids,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "top-k launch");
+  return KL_OK;
+}
+
+int kl_quantize_w8_row(const void* w, int w_dtype, int n, int k, int8_t* q, void* scale_bf16, void* stream) {
+  if (!w || !q || !scale_bf16) return fail(KL_ERR_INVALID, "null pointer");
+  if (n <= 0 || k <= 0) return fail(KL_ERR_INVALID, "weight must be a nonempty [N,K] matrix");
+  if (w_dtype < KL_DT_BF16 || w_dtype > KL_DT_F32) return fail(KL_ERR_INVALID, "weight dtype");
+  const cudaError_t e = launch_quantize_w8_row(w, w_dtype, n, k, q, scale_bf16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "quantize_w8_row");
+}
+
+int kl_quantize_w4(const void* w, int w_dtype, int n, int k, int group, int w_format, uint8_t* q, void* scales,
+                   void* zeros, void* stream) {
+  if (!w || !q || !scales) return fail(KL_ERR_INVALID, "null pointer");
+  if (!is_w4(w_format)) return fail(KL_ERR_INVALID, "w_format must be KL_W4_SYM or KL_W4_ASYM");
+  if (w_format == KL_W4_ASYM && !zeros) return fail(KL_ERR_INVALID, "zero points required");
+  if (n <= 0 || k <= 0 || group <= 0 || group % 2 || k % group)
+    return fail(KL_ERR_INVALID, "positive dimensions; an even group must divide K");
+  if (w_dtype < KL_DT_BF16 || w_dtype > KL_DT_F32) return fail(KL_ERR_INVALID, "weight dtype");
+  const cudaError_t e = launch_quantize_w4(w, w_dtype, n, k, group, w_format, q, scales, zeros,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "quantize_w4");
+}
+
+int kl_dequantize(const void* w, int w_format, int n, int k, int group, const void* scales, const void* zeros,
+                  const float* inverse, float* out, void* stream) {
+  if (!w || !out) return fail(KL_ERR_INVALID, "null pointer");
+  if (n <= 0 || k <= 0) return fail(KL_ERR_INVALID, "dimensions must be positive");
+  if (w_format < KL_W8_ROW || w_format > KL_BF16_DENSE) return fail(KL_ERR_INVALID, "unknown weight format");
+  if (is_grouped(w_format) && (group <= 0 || k % group)) return fail(KL_ERR_INVALID, "group must divide K");
+  if (w_format != KL_BF16_DENSE && !scales) return fail(KL_ERR_INVALID, "scales required");
+  if (w_format == KL_W8_GROUP && !inverse) return fail(KL_ERR_INVALID, "inverse required");
+  if (w_format == KL_W4_ASYM && !zeros) return fail(KL_ERR_INVALID, "zeros required");
+  const cudaError_t e = launch_dequantize(w, w_format, n, k, group, scales, zeros, inverse, out,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "dequantize");
+}
+
+int kl_device_status(int device, int reset) {
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int v = 0;
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_status_word, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "device status");
+  return v;
+}
+
+int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, int sm_count, int* out) {
+  if (!out || sm_count <= 0) return fail(KL_ERR_INVALID, "out and sm_count required");
+  std::memset(out, 0, 8 * sizeof(int));
+  const int group = is_grouped(w_format) ? 128 : 0;
+  const bool tc = !(flags & KL_FLAG_FORCE_SIMT) && tc_shape_ok(k, w_format, 128) && m > 0 && n > 0;
+  if (!tc) {
+    const GemvPlan gp = plan_gemv(m, swiglu ? n / 2 : n, k, w_format, group > 0 ? group : 1, swiglu != 0, true,
+                                  sm_count);
+    out[0] = 1;
+    out[1] = gp.grid_x * gp.grid_y;
+    out[2] = gp.threads;
+    out[3] = gp.smem;
+    return KL_OK;
+  }
+  const int mm = is_w4(w_format) ? std::min(m, 64) : m;
+  const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, sm_count);
+  if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan");
+  out[0] = 2;
+  out[1] = plan.grid;
+  out[2] = kTcThreads;
+  out[3] = plan.smem;
+  out[4] = plan.n_mma;
+  out[5] = plan.stages;
+  out[6] = plan.m_tiles * plan.n_tiles;
+  out[7] = static_cast<int>(plan.units);
+  // Self-check of the stream-K partition used by the kernel.
+  const long long G = plan.grid, U = plan.units, KB = plan.kb_total;
+  long long prev_hi = 0;
+  for (long long c = 0; c < G; ++c) {
+    const long long lo = unit_lo(c, U, G), hi = unit_lo(c + 1, U, G);
+    if (lo != prev_hi || hi <= lo) return fail(KL_ERR_INVALID, "partition gap or empty range at CTA %lld", c);
+    if (unit_owner(lo, U, G) != c || unit_owner(hi - 1, U, G) != c)
+      return fail(KL_ERR_INVALID, "owner mismatch at CTA %lld", c);
+    // partial segments of this CTA: at most the first and the last
+    int partial = 0;
+    for (long long t = lo / KB; t <= (hi - 1) / KB; ++t) {
+      const long long s0 = std::max(lo, t * KB), s1 = std::min(hi, (t + 1) * KB);
+      if (!(s0 == t * KB && s1 == (t + 1) * KB)) ++partial;
+    }
+    if (partial > 2) return fail(KL_ERR_INVALID, "CTA %lld has %d partial tiles", c, partial);
+    prev_hi = hi;
+  }
+  if (prev_hi != U) return fail(KL_ERR_INVALID, "partition does not cover all units");
+  const size_t ws_need = kCounterBytes + static_cast<size_t>(G) * 2 * plan.n_mma * 128 * sizeof(float);
+  if (plan.workspace < ws_need) return fail(KL_ERR_INVALID, "workspace too small for the partition");
+  return KL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,262 @@
+// Shared device helpers for the B200 (sm_100a) quantized-linear kernels:
+// status codes, bf16 bit tricks, and thin inline-PTX wrappers for mbarriers,
+// TMA (cp.async.bulk.tensor), tcgen05 (TMEM alloc / ld / st / mma / commit)
+// and programmatic dependent launch.  Every spin-wait here is bounded: it
+// gives up after a wall-clock limit, records an error code in a device status
+// word and returns false, so no kernel in this library can hang a GPU.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/kl_b200.h"
+
+#define KL_DEVICE __device__ __forceinline__
+
+namespace kl {
+
+// Wall-clock limit for any single wait inside a kernel (nanoseconds).  Normal
+// waits last nanoseconds to microseconds; this only fires if a producer never
+// arrives (a logic error), turning a would-be hang into an error status.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
+
+KL_DEVICE unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Record a KL_ERR_* code in the device status word (first error wins).
+KL_DEVICE void record_error(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+KL_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+KL_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+KL_DEVICE void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+KL_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+KL_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+KL_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Wait, bounded by time only, for the phase with the given parity to complete
+// (used on teardown paths).  Returns false if the limit passed first.
+KL_DEVICE bool mbar_wait_time(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// ----------------------------------------------------------------------- TMA
+KL_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+KL_DEVICE void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" :: "l"(map) : "memory");
+}
+
+// -------------------------------------------------- programmatic dependent launch
+KL_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+KL_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ------------------------------------------------------------------- tcgen05
+KL_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst_smem), "r"(ncols) : "memory");
+}
+KL_DEVICE void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+KL_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+KL_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+KL_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+KL_DEVICE void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+KL_DEVICE void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem desc]; kind::f16 (bf16/f16 inputs, f32 accumulate).
+KL_DEVICE void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+      :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive (once) on an mbarrier when all previously issued tcgen05 ops of this thread complete.
+KL_DEVICE void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns per thread.
+KL_DEVICE void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+KL_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for tcgen05 (K-major operand, 128-byte
+// swizzle, 8-row x 128-byte atoms stacked at 1024-byte stride).
+//   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4
+//   bits 32-45 stride byte offset >> 4  bits 46-47 version (1 on sm_100)
+//   bits 49-51 base offset (0: atoms are 1024-byte aligned)
+//   bits 61-63 layout (2 = SWIZZLE_128B)
+KL_DEVICE uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;                    // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;            // SBO = 1024 B
+  d |= static_cast<uint64_t>(1u) << 46;                    // version
+  d |= static_cast<uint64_t>(2u) << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, A and B both bf16 (or both
+// f16), both K-major, shape M x N.
+//   bits 4-5 D format (1 = f32)   bits 7-9 A format   bits 10-12 B format
+//   (0 = f16, 1 = bf16)  bit 15/16 A/B major (0 = K)  bits 17-22 N >> 3
+//   bits 24-28 M >> 4
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------- int -> bf16 bits
+KL_DEVICE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+template <int LUT>
+KL_DEVICE uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+  return d;
+}
+KL_DEVICE uint32_t fma_bf16x2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+KL_DEVICE uint32_t fma_f16x2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Four signed int8 values (one 32-bit word, byte i = element i) -> two packed
+// bf16x2 words holding the same integers exactly: {e0,e1} and {e2,e3}.
+// With v = q & 0x7F and s = q & 0x80, the bf16 bit patterns 0x4300|v and
+// 0x4300|s are the numbers 128+v and 128+2s/... (128 or 256), so
+// (0x4300|v) - (0x4300|s) = v - 128*[s != 0] = q, computed exactly by one
+// bf16x2 fma with multiplier -1.
+KL_DEVICE void s8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t t0 = prmt(w, 0x43434343u, 0x4140u);   // [e0, 43, e1, 43]
+  const uint32_t t1 = prmt(w, 0x43434343u, 0x4342u);   // [e2, 43, e3, 43]
+  // a = t & 0xFF7FFF7F ; b = (t & 0x00800080) | 0x43004300
+  const uint32_t a0 = t0 & 0xFF7FFF7Fu, a1 = t1 & 0xFF7FFF7Fu;
+  const uint32_t b0 = lop3<0xEA>(t0, 0x00800080u, 0x43004300u);
+  const uint32_t b1 = lop3<0xEA>(t1, 0x00800080u, 0x43004300u);
+  lo = fma_bf16x2(b0, 0xBF80BF80u, a0);                 // a - b
+  hi = fma_bf16x2(b1, 0xBF80BF80u, a1);
+}
+// Same for f16: 0x6400|u is 1024+u for u < 1024; u = q ^ 0x80 = q + 128.
+KL_DEVICE void s8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t t0 = prmt(u, 0x64646464u, 0x4140u);
+  const uint32_t t1 = prmt(u, 0x64646464u, 0x4342u);
+  // t - 1152 (0x6480 = 1152 in f16)
+  lo = fma_f16x2(t0, 0x3C003C00u, 0xE480E480u);
+  hi = fma_f16x2(t1, 0x3C003C00u, 0xE480E480u);
+}
+
+// Byte i of a word of 4-bit codes (low nibble = even k) -> {lo - z, hi - z}.
+// With s = w >> 4, prmt(w, s, sel_i) puts byte i of w in the low half and
+// byte i of s (whose low nibble is the high nibble of byte i of w) in the high
+// half.  Masking to the low nibble of each half and XOR-ing in the magic 0x43
+// (bf16: 0x43.0n = 128 + n) gives {128+lo, 128+hi}; one fma adds -(128 + z).
+// `magic_xor` = 0x43004300 for unsigned codes; 0x43084308 also flips nibble
+// bit 3, mapping two's-complement codes c to c + 8, so the symmetric format is
+// the same conversion with z = 8.  All results are small integers: exact.
+KL_DEVICE constexpr uint32_t nib_sel(int i) {
+  return static_cast<uint32_t>(i | (i << 4) | ((4 + i) << 8) | ((4 + i) << 12));
+}
+KL_DEVICE uint32_t u4x2_to_bf16x2(uint32_t w, uint32_t s, uint32_t sel, uint32_t magic_xor, uint32_t bias) {
+  const uint32_t t = prmt(w, s, sel);
+  const uint32_t m = lop3<0x6A>(t, 0x000F000Fu, magic_xor);   // (t & 0x000F000F) ^ magic
+  return fma_bf16x2(m, 0x3F803F80u, bias);                    // m * 1 + bias
+}
+// f16 variant: 0x64.0n = 1024 + n; magic_xor 0x64006400 / 0x64086408.
+KL_DEVICE uint32_t u4x2_to_f16x2(uint32_t w, uint32_t s, uint32_t sel, uint32_t magic_xor, uint32_t bias) {
+  const uint32_t t = prmt(w, s, sel);
+  const uint32_t m = lop3<0x6A>(t, 0x000F000Fu, magic_xor);
+  return fma_f16x2(m, 0x3C003C00u, bias);
+}
+
+KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+KL_DEVICE uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Round f32 to the activation dtype and back (bf16 when BF16, else f16).
+template <bool BF16>
+KL_DEVICE float round_act(float v) {
+  if constexpr (BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  else return __half2float(__float2half_rn(v));
+}
+template <bool BF16>
+KL_DEVICE void store_act(void* base, long long idx, float v) {
+  if constexpr (BF16) reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+  else reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+}
+template <bool BF16>
+KL_DEVICE float load_act(const void* base, long long idx) {
+  if constexpr (BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+  else return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+}
+
+// Model-ordered SwiGLU epilogue (bf16 boundaries after each projection and
+// after SiLU), the contract of the reference's fused gate/up kernels.
+template <bool BF16>
+KL_DEVICE float swiglu_model_ordered(float gate, float up) {
+  gate = round_act<BF16>(gate);
+  up = round_act<BF16>(up);
+  const float act = round_act<BF16>(gate / (1.0f + expf(-gate)));
+  return act * up;
+}
+
+}  // namespace kl

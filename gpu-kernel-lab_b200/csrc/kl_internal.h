@@ -1,0 +1,83 @@
+// Host/device structures shared by the kernels and the C-ABI dispatch layer.
+#pragma once
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace kl {
+
+// ---------------------------------------------------------------- SIMT GEMV
+struct GemvArgs {
+  const void* x;          // [M, K] activations (bf16 / f16)
+  const void* w;          // weights, per format
+  const void* scales;
+  const void* zeros;
+  const float* inverse;
+  void* y;                // [M, n_out] or [n_out, M]
+  int m, k, n_out, group, kpad, y_transposed;
+  long long ldy;          // y row stride (n_out, or the full M when transposed)
+};
+struct GemvPlan {
+  bool vec;               // 16-byte vector kernel (else scalar)
+  int mt, grid_x, grid_y, threads, smem, kpad;
+};
+int chunk_elems(int fmt);
+GemvPlan plan_gemv(int m, int n_out, int k, int fmt, int group, bool swiglu, bool aligned, int sm_count);
+cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& p, int fmt, bool swiglu, bool xbf16, cudaStream_t s);
+
+// ------------------------------------------------------------ tcgen05 GEMM
+// Swap-AB weight-only GEMM: D[n, m] = W[n, :] . X[m, :] with W (128 rows per
+// tile) converted to bf16/f16 into tensor memory as the MMA's A operand and X
+// (n_mma tokens per tile) TMA-staged in shared memory as the B operand.
+constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
+constexpr int kTcKBlock = 128;        // K elements per pipeline stage
+constexpr int kTcThreads = 320;       // 10 warps: TMA, MMA, 4 converter, 4 epilogue
+constexpr int kCounterBytes = 64 * 1024;
+constexpr int kMaxDevices = 64;
+
+struct TcParams {
+  CUtensorMap tmap_w;                 // int8 [N, K] (box 128 B x 64 rows) or u8 [N, K/2] (64 B x 64 rows)
+  CUtensorMap tmap_x;                 // bf16/f16 [M, K] (box 64 elems x n_mma rows), 128B swizzle
+  const void* scales;                 // KL_W8_ROW: bf16 [N]; KL_W4_*: per group
+  const void* zeros;                  // KL_W4_ASYM: bf16 [N, K/128]
+  void* y;
+  float* partials;                    // [grid][2][n_mma][128] f32
+  int* counters;                      // [grid] split-tile arrival counters (zero between calls)
+  int m, n, k, n_out;                 // n = weight rows, n_out = output columns
+  int m_tiles, n_tiles, kb_total;     // kb_total = k blocks per tile
+  long long units;                    // tiles * kb_total
+  int y_transposed;
+  long long ldy;                      // y row stride: n_out ([M, n_out]) or full M ([n_out, M])
+  int* status;                        // device status word (bounded-wait failures)
+};
+
+struct TcPlan {
+  bool ok;
+  int n_mma, stages, a_stages, grid, smem, tmem_cols;
+  int m_tiles, n_tiles, kb_total;
+  long long units;
+  size_t workspace;                   // counters + partials
+};
+TcPlan plan_tc(int m, int n, int k, int fmt, bool swiglu, int sm_count);
+cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
+
+// Work partition shared by the kernel and the host-side self-check:
+// CTA c owns units [lo(c), lo(c+1)) with lo(c) = floor(c * units / grid).
+__host__ __device__ inline long long unit_lo(long long c, long long units, long long grid) {
+  return (c * units) / grid;
+}
+// Owner CTA of unit u: the largest c with lo(c) <= u.
+__host__ __device__ inline long long unit_owner(long long u, long long units, long long grid) {
+  return ((u + 1) * grid + units - 1) / units - 1;
+}
+
+// ---------------------------------------------------------- quantisation
+cudaError_t launch_quantize_w8_row(const void* w, int w_dtype, int n, int k, int8_t* q, void* scale, cudaStream_t s);
+cudaError_t launch_quantize_w4(const void* w, int w_dtype, int n, int k, int group, int fmt,
+                               uint8_t* q, void* scales, void* zeros, cudaStream_t s);
+cudaError_t launch_dequantize(const void* w, int fmt, int n, int k, int group, const void* scales,
+                              const void* zeros, const float* inverse, float* out, cudaStream_t s);
+
+}  // namespace kl

@@ -1,0 +1,147 @@
+"""The quantized linear layer: ``quant_linear`` and the ``QuantLinear`` module.
+
+``quant_linear(x, weight)`` is ``F.linear(x, dequant(weight))`` for any leading
+shape of ``x`` -- the call the reference's serving executor and model
+adapters make at the QKV / o / gate_up / down / lm_head sites
+(``serving/qwen_executor.py:173,227,231-232,238``;
+``profiling/decode_stage2_ablation.py:78-143``) -- executed by the native
+B200 kernels through ``kl_linear``:
+
+* M <= 64 tokens (decode): the tcgen05 swap-AB GEMM streams the quantised
+  weights once (HBM-bound), or the CUDA-core GEMV for formats/shapes the
+  tensor-core kernel does not take;
+* M > 64 (prefill): the same tcgen05 kernel with 128-token tiles (tensor-bound).
+
+``swiglu=True`` treats the weight as ``[gate; up]`` (gate rows first) and
+returns the model-ordered ``silu(gate) * up`` in one launch.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import _native as N
+from .activation_int8 import CalibratedInt8, RowwiseInt8, quantize_int8_rowwise
+from .quantization import PackedInt4, PackedInt4Asym, quantize_int4, quantize_int4_asym
+
+
+def weight_spec(weight):
+    """(format code, data, scales, zeros, inverse, n, k, group) of a weight object."""
+    if isinstance(weight, RowwiseInt8):
+        n, k = weight.data.shape
+        return N.KL_W8_ROW, weight.data, weight.scales, None, None, n, k, k
+    if isinstance(weight, PackedInt4Asym):
+        n, k = weight.shape
+        return N.KL_W4_ASYM, weight.data, weight.scales, weight.zeros, None, n, k, weight.group_size
+    if isinstance(weight, PackedInt4):
+        n, k = weight.shape
+        return N.KL_W4_SYM, weight.data, weight.scales, None, None, n, k, weight.group_size
+    if isinstance(weight, CalibratedInt8) or all(hasattr(weight, a) for a in ("data", "scales", "inverse", "group_size")):
+        n, k = weight.data.shape
+        return N.KL_W8_GROUP, weight.data, weight.scales, None, weight.inverse, n, k, weight.group_size
+    if isinstance(weight, torch.Tensor):
+        if weight.dtype != torch.bfloat16:
+            raise RuntimeError("BF16 or INT8 weights required")
+        n, k = weight.shape
+        return N.KL_BF16_DENSE, weight, None, None, None, n, k, k
+    raise TypeError(f"unsupported weight type {type(weight).__name__}")
+
+
+def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Tensor | None = None,
+                 transposed: bool = False, pdl: bool = False, path: str | None = None,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``y = x @ dequant(weight)^T`` (f32 accumulation, output in x's dtype).
+
+    x: [..., K] bf16/f16 CUDA tensor.  Returns [..., N_out] (N_out = N, or N/2
+    with ``swiglu``), or [N_out, M] when ``transposed`` (x flattened to [M, K]).
+    ``path``: None (automatic), "tc" (tcgen05 only) or "simt" (CUDA cores only).
+    ``pdl``: launch with programmatic dependent launch (use inside a chain of
+    launches / a CUDA graph to overlap weight prefetch with the previous kernel).
+    """
+    fmt, data, scales, zeros, inverse, n, k, group = weight_spec(weight)
+    if torch.is_grad_enabled() and x.requires_grad:
+        raise ValueError("inference only")
+    if not x.is_cuda or data.device != x.device:
+        raise RuntimeError("x and the weight must be on the same CUDA device")
+    if x.shape[-1] != k:
+        raise RuntimeError(f"input K {x.shape[-1]} does not match weight K {k}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError("activations must be BF16 or FP16")
+    lead = x.shape[:-1]
+    m = 1
+    for d in lead:
+        m *= d
+    x2 = x.reshape(m, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    n_out = n // 2 if swiglu else n
+    shape = (n_out, m) if transposed else (*lead, n_out)
+    if out is None:
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    elif tuple(out.shape) != tuple(shape) or out.dtype != x.dtype or not out.is_contiguous():
+        raise RuntimeError("out has the wrong shape, dtype or layout")
+    if m == 0:
+        return out
+    flags = (N.KL_FLAG_PDL if pdl else 0) | (N.KL_FLAG_Y_TRANSPOSED if transposed else 0)
+    if path == "tc":
+        flags |= N.KL_FLAG_FORCE_TC
+    elif path == "simt":
+        flags |= N.KL_FLAG_FORCE_SIMT
+    lib = N.lib()
+    with torch.cuda.device(x.device):
+        if workspace is None:
+            need = lib.kl_linear_workspace_bytes(m, n, k, fmt, int(swiglu), flags)
+            ws = N.workspace(x.device, need)
+        else:
+            ws = workspace
+        N.check(lib.kl_linear(
+            N.ptr(x2), N.act_dtype_code(x.dtype), m, k, N.ptr(data), fmt, n, group,
+            N.ptr(scales), N.ptr(zeros), N.ptr(inverse), int(swiglu), N.ptr(out),
+            N.ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(), flags,
+            N.stream_handle(x.device)))
+    return out
+
+
+class QuantLinear(nn.Module):
+    """Bias-free ``nn.Linear`` replacement holding quantised weights only.
+
+    Formats: ``"w8_row"`` (int8 + bf16 per-row scale),
+    ``"w4_asym"`` (group-128 asymmetric int4),
+    ``"w4_sym"`` (the reference's symmetric int4).  ``swiglu=True`` makes the
+    module compute ``silu(gate) * up`` from a stacked ``[gate; up]`` weight.
+    """
+
+    def __init__(self, weight, *, swiglu: bool = False):
+        super().__init__()
+        self.weight_q = weight
+        self.swiglu = swiglu
+        fmt, data, *_rest = weight_spec(weight)
+        n, k = _rest[3], _rest[4]
+        self.in_features = k
+        self.out_features = n // 2 if swiglu else n
+        self.format = fmt
+
+    @classmethod
+    def from_weight(cls, weight: torch.Tensor, fmt: str = "w8_row", group_size: int = 128, *, swiglu: bool = False):
+        w = weight.detach()
+        if fmt == "w8_row":
+            q = quantize_int8_rowwise(w)
+        elif fmt == "w4_asym":
+            q = quantize_int4_asym(w, group_size)
+        elif fmt == "w4_sym":
+            q = quantize_int4(w, group_size)
+        else:
+            raise ValueError(f"unknown format {fmt!r}")
+        return cls(q, swiglu=swiglu)
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear, fmt: str = "w8_row", group_size: int = 128):
+        if linear.bias is not None:
+            raise ValueError("bias-free projections required")
+        return cls.from_weight(linear.weight, fmt, group_size)
+
+    def forward(self, x):
+        return quant_linear(x, self.weight_q, swiglu=self.swiglu)
+
+    def extra_repr(self):
+        return f"in_features={self.in_features}, out_features={self.out_features}, format={self.format}, swiglu={self.swiglu}"

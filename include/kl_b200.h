@@ -1,0 +1,157 @@
+/*
+ * kl_b200.h -- C ABI of the B200 (sm_100a) weight-only quantized linear layer.
+ *
+ * Plain C: pointers, sizes and integer flags only; no framework types.  All
+ * tensor pointers are DEVICE pointers (the caller owns every buffer), except
+ * where a comment says otherwise.  `stream` is a cudaStream_t passed as void*
+ * (NULL = the legacy default stream).  Every entry point returns a KL_* status
+ * and never aborts the process; nothing here allocates device memory, so the
+ * calls are safe inside CUDA-graph stream capture.
+ *
+ * Reference interfaces replaced (paths inside yashlabs-trying/gpu-kernel-lab):
+ *   kl_project            <- learning/10_cuda_decode/warp_gemv.cu:56-90  project(x, w, scales,
+ *                            inverse, group, warps, persistent, swiglu) (the pybind op, :91)
+ *   kl_linear             <- the F.linear call sites the W8A16 op replaces:
+ *                            serving/qwen_executor.py:173,227,231-232,238 and the
+ *                            nn.Linear patches of profiling/decode_stage2_ablation.py:78-84
+ *                            (same math as kl_project, generalised to x[M,K] and all formats)
+ *   kl_int4_gemv          <- learning/09_int4/kernels.py:67-74      int4_gemv(x, packed, block_n)
+ *   kl_int4_lm_head_topk  <- learning/09_int4/kernels.py:77-99      int4_lm_head_topk(...)
+ *   kl_quantize_w8_row    <- learning/10_cuda_decode/activation_int8.py:47-52 with group = K,
+ *                            alpha 0, bf16 scale (the BASELINE.json config 0 format)
+ *   kl_quantize_w4        <- learning/09_int4/quantization.py:35-62 quantize_int4 (KL_W4_SYM),
+ *                            and its asymmetric bf16 scale/zero sibling (KL_W4_ASYM)
+ *   kl_dequantize         <- learning/10_cuda_decode/activation_int8.py:63-64 dequantize_int8,
+ *                            learning/09_int4/quantization.py:65-71 dequantize_int4
+ */
+#ifndef KL_B200_H
+#define KL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define KL_OK              0
+#define KL_ERR_INVALID     1  /* bad argument: shape, dtype, alignment, flag      */
+#define KL_ERR_UNSUPPORTED 2  /* valid request this device/build cannot run       */
+#define KL_ERR_CUDA        3  /* a CUDA runtime / driver call failed              */
+#define KL_ERR_WORKSPACE   4  /* workspace missing or smaller than required       */
+#define KL_ERR_TIMEOUT     5  /* a bounded in-kernel wait gave up (device status) */
+
+/* ---- element types --------------------------------------------------- */
+#define KL_DT_BF16 0
+#define KL_DT_F16  1
+#define KL_DT_F32  2
+
+/* ---- weight formats (all row-major [N, K] along K) ------------------- */
+#define KL_W8_ROW     0 /* int8 q[N,K]; bf16 scale[N]:               w = q * s[n]           */
+#define KL_W8_GROUP   1 /* int8 q[N,K]; f32 scales[N,K/g], f32 inverse[K]:
+                           w = q * s[n,k/g] * inverse[k]  (reference CalibratedInt8)       */
+#define KL_W4_SYM     2 /* uint8 [N,K/2] two's-complement nibbles, low nibble = even k;
+                           f32 scales[N,K/g]: w = c * s  (reference PackedInt4)            */
+#define KL_W4_ASYM    3 /* uint8 [N,K/2] unsigned nibbles, low = even k; bf16 scales and
+                           bf16 zeros [N,K/g]:  w = (q - z) * s                            */
+#define KL_BF16_DENSE 4 /* bf16 w[N,K] (reference project() with a BF16 weight)          */
+
+/* ---- kl_linear flags ------------------------------------------------- */
+#define KL_FLAG_FORCE_SIMT    1 /* use the CUDA-core kernel even where tcgen05 applies    */
+#define KL_FLAG_FORCE_TC      2 /* require the tcgen05 kernel (KL_ERR_UNSUPPORTED if not)  */
+#define KL_FLAG_PDL           4 /* launch with programmatic dependent launch (overlaps the
+                                   weight prefetch with the previous kernel on the stream) */
+#define KL_FLAG_Y_TRANSPOSED  8 /* write y as [N_out, M] (m contiguous) instead of [M, N_out] */
+
+/*
+ * y = x @ dequant(w)^T   (optionally SwiGLU-fused), fp32 accumulation,
+ * output rounded to the activation dtype.
+ *   x      [M, K] contiguous, KL_DT_BF16 or KL_DT_F16
+ *   w      per w_format; n = weight rows; group = K-group of the scales
+ *          (ignored for KL_W8_ROW / KL_BF16_DENSE)
+ *   swiglu 0: y is [M, N];  1: gate rows [0, N/2) precede up rows [N/2, N) and
+ *          y = bf16(bf16(silu(bf16(gate))) * bf16(up)) is [M, N/2]
+ *   workspace  device scratch of kl_linear_workspace_bytes(...) bytes; its first
+ *          64 KiB must be zero before the first call on that buffer (the kernels
+ *          leave it zero again).  May be NULL when that size is 0.  Calls that
+ *          share a workspace must not run concurrently.
+ */
+int kl_linear(const void* x, int x_dtype, int m, int k,
+              const void* w, int w_format, int n, int group,
+              const void* scales, const void* zeros, const float* inverse,
+              int swiglu, void* y, void* workspace, size_t workspace_bytes,
+              int flags, void* stream);
+
+/* Bytes of workspace kl_linear needs for this problem (0 if none). */
+size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, int flags);
+
+/*
+ * The reference's op, same arguments and checks (warp_gemv.cu:56-72):
+ *   x bf16 [K]; w int8 [N,K] (w_is_int8 = 1, with f32 scales [N,K/group] and
+ *   f32 inverse [K]) or bf16 [N,K] (w_is_int8 = 0, scales/inverse ignored);
+ *   warps must be 1, 4 or 8; swiglu requires an even N.  y bf16 [N] or [N/2].
+ * `warps` / `persistent` are accepted for interface compatibility; the launch
+ * geometry is chosen for the B200.
+ */
+int kl_project(const void* x, int k, const void* w, int w_is_int8,
+               const float* scales, const float* inverse, int n, int group,
+               int warps, int persistent, int swiglu, void* y,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* int4_gemv(x, packed, block_n): x bf16/f16 [K]; w KL_W4_SYM; y [N] in x's dtype. */
+int kl_int4_gemv(const void* x, int x_dtype, int k, const uint8_t* w, const float* scales,
+                 int n, int group, int block_n, void* y, void* stream);
+
+/*
+ * int4_lm_head_topk(x, packed, top_k, block_n): fused lm_head projection with
+ * tile-local top-k and a global merge.  values f32 [top_k], ids int64 [top_k]
+ * (descending; top-1 ties resolve to the lowest vocabulary index).
+ * workspace: kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n) bytes.
+ */
+int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w,
+                         const float* scales, int n, int group, int top_k, int block_n,
+                         float* values, int64_t* ids, void* workspace,
+                         size_t workspace_bytes, void* stream);
+size_t kl_int4_lm_head_topk_workspace_bytes(int n, int top_k, int block_n);
+
+/* Per-row W8 quantiser: w [N,K] (KL_DT_F32/BF16/F16) -> q int8 [N,K], scale bf16 [N]. */
+int kl_quantize_w8_row(const void* w, int w_dtype, int n, int k,
+                       int8_t* q, void* scale_bf16, void* stream);
+
+/* 4-bit quantiser, w_format KL_W4_SYM (scales f32, zeros unused) or KL_W4_ASYM
+ * (scales and zeros bf16).  q uint8 [N, K/2]. */
+int kl_quantize_w4(const void* w, int w_dtype, int n, int k, int group, int w_format,
+                   uint8_t* q, void* scales, void* zeros, void* stream);
+
+/* Dequantise any format to f32 out[N,K] with the exact arithmetic the GEMM
+ * kernels use (bit-exact against the reference dequantisers). */
+int kl_dequantize(const void* w, int w_format, int n, int k, int group,
+                  const void* scales, const void* zeros, const float* inverse,
+                  float* out, void* stream);
+
+/* ---- diagnostics -------------------------------------------------------- */
+const char* kl_status_string(int status);
+/* Message describing the last non-OK status returned on the calling thread. */
+const char* kl_last_error(void);
+/* Reads the device status word set by bounded in-kernel waits (synchronises
+ * the device); reset != 0 clears it.  Returns a KL_* code. */
+int kl_device_status(int device, int reset);
+/* Version of this library: major*10000 + minor*100 + patch. */
+int kl_version(void);
+
+/*
+ * Host-only description of the launch plan kl_linear would use on a device
+ * with `sm_count` SMs, and a self-check of its work partition (every
+ * (tile, k-block) unit covered exactly once, workspace slots in bounds).
+ * Needs no GPU.  Returns KL_OK and fills `out` (array of 8 ints:
+ * kernel (0 none, 1 simt, 2 tcgen05), grid, threads, smem bytes,
+ * n_mma (tcgen05 token tile), stages, tiles, units).
+ */
+int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags,
+                     int sm_count, int* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KL_B200_H */

@@ -1,0 +1,92 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the header
+declares, and the host-side launch planner partitions every BASELINE shape
+correctly (no GPU needed)."""
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+QWEN = [(4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (151936, 1024)]
+LLAMA = [(5120, 3072), (3072, 3072), (16384, 3072), (3072, 8192), (128256, 3072)]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "kl_b200.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(kl_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_header_symbol(kl):
+    lib = kl._native.lib()
+    declared = header_symbols()
+    assert declared, "no declarations parsed from the header"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in kl_b200.h but not exported"
+    assert set(declared) == set(kl._native.EXPORTED_SYMBOLS)
+    assert lib.kl_version() >= 100
+
+
+def test_status_strings(kl):
+    lib = kl._native.lib()
+    assert lib.kl_status_string(0) == b"ok"
+    assert b"invalid" in lib.kl_status_string(1)
+    assert b"workspace" in lib.kl_status_string(4)
+    assert b"timed out" in lib.kl_status_string(5)
+
+
+def test_validation_needs_no_gpu(kl):
+    """Argument checks run before any CUDA call: bad shapes fail on a CPU box."""
+    lib = kl._native.lib()
+    N = kl._native
+    # null pointers
+    assert lib.kl_linear(None, 0, 1, 16, None, N.KL_W8_ROW, 16, 16, None, None, None, 0, None, None, 0, 0, None) == N.KL_ERR_INVALID
+    assert b"non-null" in lib.kl_last_error()
+    # reference op: warps must be 1/4/8, swiglu needs an even N
+    fake = 256
+    assert lib.kl_project(fake, 16, fake, 0, None, None, 8, 16, 2, 0, 0, fake, None, 0, None) == N.KL_ERR_INVALID
+    assert b"warps" in lib.kl_last_error()
+    assert lib.kl_project(fake, 16, fake, 0, None, None, 7, 16, 4, 0, 1, fake, None, 0, None) == N.KL_ERR_INVALID
+    assert b"gate/up" in lib.kl_last_error()
+    # int4 reference op: group and block_n domains
+    assert lib.kl_int4_gemv(fake, 0, 128, fake, fake, 8, 48, 32, fake, None) == N.KL_ERR_INVALID
+    assert lib.kl_int4_gemv(fake, 0, 128, fake, fake, 8, 128, 24, fake, None) == N.KL_ERR_INVALID
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 256, 512, 2048, 8192])
+@pytest.mark.parametrize("n,k", QWEN + LLAMA)
+def test_plan_partition_w8(kl, m, n, k):
+    plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, sm_count=148)
+    assert plan["kernel"] == 2
+    assert 1 <= plan["grid"] <= 148
+    assert plan["smem"] <= 227 * 1024
+    assert plan["n_mma"] in (16, 32, 64, 128)
+    if m <= 64:
+        assert plan["smem"] <= 110 * 1024   # leaves room for the next kernel's CTA (PDL overlap)
+
+
+@pytest.mark.parametrize("m", [1, 16, 64])
+@pytest.mark.parametrize("n,k", [(6144, 1024), (12288, 1024), (16384, 3072)])
+def test_plan_partition_swiglu(kl, m, n, k):
+    plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, swiglu=True, sm_count=148)
+    assert plan["kernel"] == 2 and plan["tiles"] == ((n // 2 + 63) // 64) * ((m + plan["n_mma"] - 1) // plan["n_mma"])
+
+
+@pytest.mark.parametrize("m", [1, 16, 200])
+@pytest.mark.parametrize("n,k", QWEN)
+def test_plan_partition_w4(kl, m, n, k):
+    plan = kl._native.describe_plan(m, n, k, kl._native.KL_W4_ASYM, sm_count=148)
+    assert plan["kernel"] == 2 and plan["n_mma"] <= 64
+
+
+@pytest.mark.parametrize("sm", [1, 7, 132, 148, 296])
+def test_plan_partition_odd_grids(kl, sm):
+    for n, k in [(17, 128), (1024, 1024), (151936, 1024)]:
+        kl._native.describe_plan(3, n, k, kl._native.KL_W8_ROW, sm_count=sm)
+
+
+def test_simt_plan_for_reference_formats(kl):
+    N = kl._native
+    assert N.describe_plan(1, 34, 256, N.KL_W8_GROUP)["kernel"] == 1
+    assert N.describe_plan(1, 33, 7, N.KL_BF16_DENSE)["kernel"] == 1
+    assert N.describe_plan(1, 17, 128, N.KL_W4_SYM, flags=N.KL_FLAG_FORCE_SIMT)["kernel"] == 1
