@@ -15,7 +15,7 @@ from .activation_int8 import (CalibratedInt8, RowwiseInt8, dequantize_int8, dequ
                               quantize_int8, quantize_int8_rowwise)
 from .cuda_decode import extension, project
 from .kernels import int4_gemv, int4_lm_head_topk
-from .linear import QuantLinear, quant_linear, weight_spec
+from .linear import GroupedLinear, QuantLinear, quant_linear, weight_spec
 from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequantize_int4_asym, quantize_int4,
                            quantize_int4_asym)
 from .native_ops import dequantize_native
@@ -24,6 +24,6 @@ __all__ = [
     "CalibratedInt8", "RowwiseInt8", "PackedInt4", "PackedInt4Asym", "QuantLinear",
     "quantize_int8", "dequantize_int8", "quantize_int8_rowwise", "dequantize_int8_rowwise",
     "quantize_int4", "dequantize_int4", "quantize_int4_asym", "dequantize_int4_asym",
-    "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec",
+    "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec", "GroupedLinear",
     "dequantize_native",
 ]

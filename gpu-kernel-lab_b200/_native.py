@@ -26,7 +26,15 @@ EXPORTED_SYMBOLS = (
     "kl_int4_lm_head_topk", "kl_int4_lm_head_topk_workspace_bytes", "kl_quantize_w8_row",
     "kl_quantize_w4", "kl_dequantize", "kl_status_string", "kl_last_error",
     "kl_device_status", "kl_version", "kl_describe_plan",
+    "kl_grouped_table_bytes", "kl_grouped_encode", "kl_grouped_workspace_bytes", "kl_linear_grouped",
 )
+
+
+class KlProblem(ctypes.Structure):
+    """``kl_problem`` of include/kl_b200.h."""
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("zeros", ctypes.c_void_p), ("y", ctypes.c_void_p), ("m", ctypes.c_int), ("n", ctypes.c_int),
+                ("k", ctypes.c_int), ("group", ctypes.c_int)]
 
 _P, _I, _S = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
 _SIGNATURES = {
@@ -44,6 +52,10 @@ _SIGNATURES = {
     "kl_device_status": (_I, [_I, _I]),
     "kl_version": (_I, []),
     "kl_describe_plan": (_I, [_I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int)]),
+    "kl_grouped_table_bytes": (_S, [_I]),
+    "kl_grouped_encode": (_I, [_P, _I, _I, _I, _I, _P, _S]),
+    "kl_grouped_workspace_bytes": (_S, [_P]),
+    "kl_linear_grouped": (_I, [_P, _P, _P, _S, _I, _P]),
 }
 
 _lib = None

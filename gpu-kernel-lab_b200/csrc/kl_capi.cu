@@ -106,6 +106,44 @@ bool tc_shape_ok(int k, int w_format, int group) {
   return false;
 }
 
+// Fill one tcgen05 problem (tensor maps + fields); the caller sets unit_begin.
+int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n,
+                  const void* scales, const void* zeros, int swiglu, void* y, bool transposed, long long ldy,
+                  int n_mma) {
+  std::memset(&pr, 0, sizeof(pr));
+  int rc;
+  if (is_w4(w_format))
+    rc = encode_2d(&pr.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k / 2, n, k / 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+  else
+    rc = encode_2d(&pr.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != KL_OK) return rc;
+  rc = encode_2d(&pr.tmap_x, x_dtype == KL_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                 x, k, m, static_cast<uint64_t>(k) * act_bytes(x_dtype), 64, n_mma, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != KL_OK) return rc;
+  pr.scales = scales;
+  pr.zeros = zeros;
+  pr.y = y;
+  pr.ldy = ldy;
+  pr.m = m;
+  pr.n = n;
+  pr.k = k;
+  pr.n_out = swiglu ? n / 2 : n;
+  pr.y_transposed = transposed ? 1 : 0;
+  tc_problem_tiles(pr, n_mma, swiglu != 0);
+  return KL_OK;
+}
+
+// Units of one problem without building its tensor maps (host planning only).
+long long problem_units(int m, int n, int k, int n_mma, bool swiglu) {
+  TcProblem pr;
+  std::memset(&pr, 0, sizeof(pr));
+  pr.m = m;
+  pr.n = n;
+  pr.k = k;
+  pr.n_out = swiglu ? n / 2 : n;
+  return tc_problem_tiles(pr, n_mma, swiglu);
+}
+
 int validate_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
                     const void* scales, const void* zeros, const float* inverse, int swiglu, const void* y,
                     int flags) {
@@ -158,7 +196,8 @@ size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, 
     cudaGetLastError();
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;
-  const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, sm);
+  const int n_mma = tc_choose_nmma(mm, w_format);
+  const TcPlan plan = plan_tc(n_mma, problem_units(mm, n, k, n_mma, swiglu != 0), w_format, sm);
   return plan.ok ? plan.workspace : 0;
 }
 
@@ -186,39 +225,28 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     const int mchunk = is_w4(w_format) ? 64 : m;
     for (int m0 = 0; m0 < m; m0 += mchunk) {
       const int mm = std::min(mchunk, m - m0);
-      const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, di.sm_count);
+      const int n_mma = tc_choose_nmma(mm, w_format);
+      TcParams p;
+      std::memset(&p, 0, sizeof(p));
+      const char* xb = static_cast<const char*>(x) + static_cast<size_t>(m0) * k * eb;
+      char* yb = static_cast<char*>(y) + (transposed ? static_cast<size_t>(m0) : static_cast<size_t>(m0) * n_out) * eb;
+      rc = build_problem(p.single, xb, x_dtype, mm, k, w, w_format, n, scales, zeros, swiglu, yb, transposed,
+                         transposed ? m : n_out, n_mma);
+      if (rc != KL_OK) return rc;
+      p.single.unit_begin = 0;
+      const long long units = static_cast<long long>(p.single.m_tiles) * p.single.n_tiles * p.single.kb_total;
+      const TcPlan plan = plan_tc(n_mma, units, w_format, di.sm_count);
       if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for m=%d n=%d k=%d", mm, n, k);
       if (!workspace || workspace_bytes < plan.workspace)
         return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
                     workspace ? workspace_bytes : 0);
-      TcParams p;
-      std::memset(&p, 0, sizeof(p));
-      const char* xb = static_cast<const char*>(x) + static_cast<size_t>(m0) * k * eb;
-      if (is_w4(w_format)) {
-        rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k / 2, n, k / 2, 64, 64,
-                       CU_TENSOR_MAP_SWIZZLE_64B);
-      } else {
-        rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-      }
-      if (rc != KL_OK) return rc;
-      rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, k, mm,
-                     static_cast<uint64_t>(k) * eb, 64, plan.n_mma, CU_TENSOR_MAP_SWIZZLE_128B);
-      if (rc != KL_OK) return rc;
-      p.scales = scales;
-      p.zeros = zeros;
-      p.y = static_cast<char*>(y) + (transposed ? static_cast<size_t>(m0) : static_cast<size_t>(m0) * n_out) * eb;
+      p.table = nullptr;
+      p.count = 1;
+      p.w_stages = plan.w_stages;
+      p.x_stages = plan.x_stages;
+      p.units = units;
       p.counters = static_cast<int*>(workspace);
       p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
-      p.m = mm;
-      p.n = n;
-      p.k = k;
-      p.n_out = n_out;
-      p.m_tiles = plan.m_tiles;
-      p.n_tiles = plan.n_tiles;
-      p.kb_total = plan.kb_total;
-      p.units = plan.units;
-      p.y_transposed = transposed ? 1 : 0;
-      p.ldy = transposed ? m : n_out;
       p.status = di.status;
       const cudaError_t e = launch_tc(p, plan, w_format, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
       if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
@@ -243,6 +271,114 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
   a.ldy = transposed ? m : n_out;
   const cudaError_t e = launch_gemv(a, gp, w_format, swiglu != 0, xbf16, s);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  return KL_OK;
+}
+
+namespace {
+struct GroupHeader {
+  uint32_t magic, count;
+  int n_mma, w_format, swiglu, x_dtype;
+  long long units;
+  uint8_t pad[256 - 32];
+};
+static_assert(sizeof(GroupHeader) == 256, "group header");
+constexpr uint32_t kGroupMagic = 0x4B4C4752u;   // "KLGR"
+}  // namespace
+
+size_t kl_grouped_table_bytes(int count) {
+  if (count <= 0 || count > kMaxGroup) return 0;
+  return sizeof(GroupHeader) + static_cast<size_t>(count) * sizeof(TcProblem);
+}
+
+int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_format, int swiglu, void* host_table,
+                      size_t table_bytes) {
+  if (!problems || !host_table) return fail(KL_ERR_INVALID, "problems and host_table must be non-null");
+  if (count <= 0 || count > kMaxGroup) return fail(KL_ERR_INVALID, "count must be in [1, %d]", kMaxGroup);
+  if (table_bytes < kl_grouped_table_bytes(count)) return fail(KL_ERR_INVALID, "host table too small");
+  if (!(w_format == KL_W8_ROW || is_w4(w_format)))
+    return fail(KL_ERR_UNSUPPORTED, "grouped launches take KL_W8_ROW or the 4-bit formats");
+  int max_m = 0;
+  for (int i = 0; i < count; ++i) {
+    const kl_problem& q = problems[i];
+    const int grp = is_w4(w_format) ? q.group : q.k;
+    int rc = validate_linear(q.x, x_dtype, q.m, q.k, q.w, w_format, q.n, grp, q.scales, q.zeros, nullptr, swiglu,
+                             q.y, 0);
+    if (rc != KL_OK) return fail(rc, "problem %d: %s", i, g_last_error);
+    if (!tc_shape_ok(q.k, w_format, grp) || !aligned16(q.x) || !aligned16(q.w))
+      return fail(KL_ERR_UNSUPPORTED, "problem %d is not tcgen05-compatible (K %d, group %d, alignment)", i, q.k, grp);
+    max_m = std::max(max_m, q.m);
+  }
+  if (is_w4(w_format) && max_m > 64) return fail(KL_ERR_UNSUPPORTED, "grouped 4-bit launches take m <= 64");
+  GroupHeader* hd = static_cast<GroupHeader*>(host_table);
+  std::memset(hd, 0, sizeof(*hd));
+  hd->magic = kGroupMagic;
+  hd->count = static_cast<uint32_t>(count);
+  hd->n_mma = tc_choose_nmma(max_m, w_format);
+  hd->w_format = w_format;
+  hd->swiglu = swiglu ? 1 : 0;
+  hd->x_dtype = x_dtype;
+  TcProblem* tab = reinterpret_cast<TcProblem*>(hd + 1);
+  long long units = 0;
+  for (int i = 0; i < count; ++i) {
+    const kl_problem& q = problems[i];
+    const int n_out = swiglu ? q.n / 2 : q.n;
+    int rc = build_problem(tab[i], q.x, x_dtype, q.m, q.k, q.w, w_format, q.n, q.scales, q.zeros, swiglu, q.y, false,
+                           n_out, hd->n_mma);
+    if (rc != KL_OK) return rc;
+    tab[i].unit_begin = units;
+    units += static_cast<long long>(tab[i].m_tiles) * tab[i].n_tiles * tab[i].kb_total;
+  }
+  hd->units = units;
+  return KL_OK;
+}
+
+size_t kl_grouped_workspace_bytes(const void* host_table) {
+  const GroupHeader* hd = static_cast<const GroupHeader*>(host_table);
+  if (!hd || hd->magic != kGroupMagic) return 0;
+  int sm = 148, dev = 0, v = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+    sm = v;
+  else
+    cudaGetLastError();
+  const TcPlan plan = plan_tc(hd->n_mma, hd->units, hd->w_format, sm);
+  return plan.ok ? plan.workspace : 0;
+}
+
+int kl_linear_grouped(const void* host_table, const void* device_table, void* workspace, size_t workspace_bytes,
+                      int flags, void* stream) {
+  const GroupHeader* hd = static_cast<const GroupHeader*>(host_table);
+  if (!hd || hd->magic != kGroupMagic) return fail(KL_ERR_INVALID, "host_table was not built by kl_grouped_encode");
+  if (hd->count > 1 && (!device_table || (reinterpret_cast<uintptr_t>(device_table) & 63u)))
+    return fail(KL_ERR_INVALID, "device_table must be a 64-byte-aligned device copy of the table");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != KL_OK) return rc;
+  if (!(di.major == 10 && di.minor == 0))
+    return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
+  const TcPlan plan = plan_tc(hd->n_mma, hd->units, hd->w_format, di.sm_count);
+  if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for the group");
+  if (!workspace || workspace_bytes < plan.workspace)
+    return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
+                workspace ? workspace_bytes : 0);
+  const TcProblem* host_tab = reinterpret_cast<const TcProblem*>(hd + 1);
+  TcParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.count = static_cast<int>(hd->count);
+  if (p.count == 1) {
+    p.single = host_tab[0];
+    p.table = nullptr;
+  } else {
+    p.table = reinterpret_cast<const TcProblem*>(static_cast<const char*>(device_table) + sizeof(GroupHeader));
+  }
+  p.w_stages = plan.w_stages;
+  p.x_stages = plan.x_stages;
+  p.units = hd->units;
+  p.counters = static_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+  p.status = di.status;
+  const cudaError_t e = launch_tc(p, plan, hd->w_format, hd->swiglu != 0, hd->x_dtype == KL_DT_BF16,
+                                  (flags & KL_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "grouped tcgen05 GEMM launch");
   return KL_OK;
 }
 
@@ -364,18 +500,27 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     return KL_OK;
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;
-  const TcPlan plan = plan_tc(mm, n, k, w_format, swiglu != 0, sm_count);
+  const int n_mma = tc_choose_nmma(mm, w_format);
+  TcProblem pr;
+  std::memset(&pr, 0, sizeof(pr));
+  pr.m = mm;
+  pr.n = n;
+  pr.k = k;
+  pr.n_out = swiglu ? n / 2 : n;
+  const long long units = tc_problem_tiles(pr, n_mma, swiglu != 0);
+  const TcPlan plan = plan_tc(n_mma, units, w_format, sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan");
   out[0] = 2;
   out[1] = plan.grid;
   out[2] = kTcThreads;
   out[3] = plan.smem;
   out[4] = plan.n_mma;
-  out[5] = plan.stages;
-  out[6] = plan.m_tiles * plan.n_tiles;
+  out[5] = plan.w_stages;
+  out[6] = pr.m_tiles * pr.n_tiles;
   out[7] = static_cast<int>(plan.units);
+  const long long KB = pr.kb_total;
   // Self-check of the stream-K partition used by the kernel.
-  const long long G = plan.grid, U = plan.units, KB = plan.kb_total;
+  const long long G = plan.grid, U = plan.units;
   long long prev_hi = 0;
   for (long long c = 0; c < G; ++c) {
     const long long lo = unit_lo(c, U, G), hi = unit_lo(c + 1, U, G);

@@ -11,7 +11,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include "../../include/kl_b200.h"
+#include "kl_b200.h"
 
 #define KL_DEVICE __device__ __forceinline__
 

@@ -33,34 +33,48 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& p, int fmt, bool swig
 // (n_mma tokens per tile) TMA-staged in shared memory as the B operand.
 constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
 constexpr int kTcKBlock = 128;        // K elements per pipeline stage
-constexpr int kTcThreads = 320;       // 10 warps: TMA, MMA, 4 converter, 4 epilogue
+constexpr int kTcWarps = 15;          // W-TMA, MMA, X-TMA, 8 converter, 4 epilogue warps
+constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kCounterBytes = 64 * 1024;
 constexpr int kMaxDevices = 64;
+constexpr int kMaxGroup = 512;        // problems per grouped launch
+constexpr int kMaxWStages = 16;
 
-struct TcParams {
+// One GEMM of a launch (256-byte aligned so it can live in a device table).
+struct alignas(64) TcProblem {
   CUtensorMap tmap_w;                 // int8 [N, K] (box 128 B x 64 rows) or u8 [N, K/2] (64 B x 64 rows)
   CUtensorMap tmap_x;                 // bf16/f16 [M, K] (box 64 elems x n_mma rows), 128B swizzle
-  const void* scales;                 // KL_W8_ROW: bf16 [N]; KL_W4_*: per group
+  const void* scales;                 // KL_W8_ROW: bf16 [N]; KL_W4_*: per group of 128
   const void* zeros;                  // KL_W4_ASYM: bf16 [N, K/128]
   void* y;
-  float* partials;                    // [grid][2][n_mma][128] f32
-  int* counters;                      // [grid] split-tile arrival counters (zero between calls)
+  long long ldy;                      // y row stride: n_out ([M, n_out]) or M ([n_out, M])
+  long long unit_begin;               // first global work unit of this problem
   int m, n, k, n_out;                 // n = weight rows, n_out = output columns
   int m_tiles, n_tiles, kb_total;     // kb_total = k blocks per tile
-  long long units;                    // tiles * kb_total
   int y_transposed;
-  long long ldy;                      // y row stride: n_out ([M, n_out]) or full M ([n_out, M])
+};
+
+struct TcParams {
+  TcProblem single;                   // the problem when count == 1
+  const TcProblem* table;             // device table when count > 1
+  int count;
+  int w_stages, x_stages;
+  long long units;                    // total (tile, k-block) units over all problems
+  float* partials;                    // [grid][2][n_mma][128] f32
+  int* counters;                      // [grid] split-tile arrival counters (zero between calls)
   int* status;                        // device status word (bounded-wait failures)
 };
 
 struct TcPlan {
   bool ok;
-  int n_mma, stages, a_stages, grid, smem, tmem_cols;
-  int m_tiles, n_tiles, kb_total;
+  int n_mma, w_stages, x_stages, grid, smem;
   long long units;
   size_t workspace;                   // counters + partials
 };
-TcPlan plan_tc(int m, int n, int k, int fmt, bool swiglu, int sm_count);
+int tc_choose_nmma(int m, int fmt);
+// Fill the tiling fields of a problem (m_tiles, n_tiles, kb_total); returns its unit count.
+long long tc_problem_tiles(TcProblem& pr, int n_mma, bool swiglu);
+TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count);
 cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
 // Work partition shared by the kernel and the host-side self-check:

@@ -1,5 +1,6 @@
-// tcgen05 weight-only quantized GEMM for B200 (sm_100a): decode (M <= 64) and
-// prefill (M > 64) in one warp-specialised kernel.
+// tcgen05 weight-only quantized GEMM for B200 (sm_100a): decode (M <= 64),
+// prefill (M > 64) and grouped launches of independent GEMMs, in one
+// warp-specialised persistent kernel.
 //
 //   y[m, n] = sum_k x[m, k] * dequant(w)[n, k]      (f32 accumulate, bf16/f16 out)
 //
@@ -8,15 +9,17 @@
 // legal 128 x 16 MMA and the weight stream -- the quantity that sets the speed
 // at small M -- is read exactly once per tile.
 //
-// Data path per 128-element K block (one pipeline stage):
-//   HBM --TMA--> smem int8/int4 tile (swizzled)       [producer warp]
-//   smem --ld.shared--> registers --exact int->bf16--> tcgen05.st --> TMEM
-//                                                       [4 converter warps]
-//   tcgen05.mma.kind::f16  D[tmem] += A[tmem] * X[smem]  [1 MMA thread]
-//   TMEM --tcgen05.ld--> registers --> scale / SwiGLU --> global
-//                                                       [4 epilogue warps]
-// Converting straight into tensor memory keeps the bf16 copy of the weights
-// out of shared memory entirely: smem only carries the compressed tile once.
+// Data path per 128-element K block (one pipeline unit):
+//   HBM --TMA--> smem int8/int4 tile (swizzled)          [W producer warp]
+//   L2  --TMA--> smem x tile (swizzled, MMA B operand)    [X producer warp]
+//   smem --ld.shared--> regs --exact int->bf16--> tcgen05.st --> TMEM
+//                                                         [8 converter warps]
+//   tcgen05.mma.kind::f16  D[tmem] += A[tmem] * X[smem]    [1 MMA thread]
+//   TMEM --tcgen05.ld--> regs --> scale / SwiGLU --> global [4 epilogue warps]
+// The weight ring is released by the converters as soon as a tile is in TMEM,
+// independently of the MMA, so its depth (up to 16 x 16 KB per SM) is what
+// covers HBM latency.  Converting straight into tensor memory keeps the bf16
+// copy of the weights out of shared memory entirely.
 //
 // The integer codes are exact in bf16 (|q| <= 127 for int8, |q - z| <= 15 for
 // int4) and the per-row / per-group scales are applied to the f32 accumulator,
@@ -26,12 +29,12 @@
 //   KL_W4_ASYM / KL_W4_SYM (group 128 = one K block): every K block is a
 //   separate accumulation that the epilogue scales and adds in registers.
 //
-// Work partition (stream-K): the (tile, k-block) units are split into `grid`
-// contiguous ranges.  A tile covered by one CTA is finished in place; a tile
-// split between CTAs is finished by the last CTA to arrive (an atomic counter),
-// which sums every contributor's f32 partial in CTA order -- deterministic,
-// with no spin-wait on another CTA.  Every mbarrier wait is bounded (see
-// kl_common.cuh).
+// Work partition (stream-K): the (problem, tile, k-block) units of all
+// problems are split into `grid` contiguous ranges.  A tile covered by one CTA
+// is finished in place; a tile split between CTAs is finished by the last CTA
+// to arrive (an atomic counter), which sums every contributor's f32 partial in
+// CTA order -- deterministic, with no spin-wait on another CTA.  Every
+// mbarrier wait is bounded (see kl_common.cuh).
 #include "kl_common.cuh"
 #include "kl_internal.h"
 
@@ -43,11 +46,11 @@ namespace {
 
 template <int NMMA>
 struct TcCfg {
-  static constexpr int A_STAGES = NMMA == 128 ? 4 : (NMMA == 64 ? 2 : 3);
+  static constexpr int A_STAGES = NMMA == 128 ? 4 : 6;
   static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D buffer
   static constexpr int D_COL0 = 64 * A_STAGES;               // A stages first (64 cols each)
-  static constexpr int USED = D_COL0 + 2 * D_PITCH;
-  static constexpr int TMEM_COLS = USED <= 64 ? 64 : USED <= 128 ? 128 : USED <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(D_COL0 + 2 * D_PITCH <= TMEM_COLS, "TMEM budget");
   static constexpr int X_ATOM = NMMA * 128;                  // bytes: NMMA rows x 64 bf16
   static constexpr int X_STAGE = 2 * X_ATOM;
 };
@@ -56,20 +59,22 @@ template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL
 template <int FMT> constexpr int w_stage_bytes() { return is_w4<FMT>() ? 8192 : 16384; }
 template <int FMT> constexpr bool grouped() { return is_w4<FMT>(); }
 
-constexpr int kXchBytes = 64 * 16 * 4;   // SwiGLU up-value exchange: 64 rows x 16 cols f32
+constexpr int kXchBytes = 64 * 16 * 4;            // SwiGLU up-value exchange: 64 rows x 16 cols f32
+constexpr int kUnitCacheBytes = 8 * kMaxGroup;    // problem unit_begin cache (grouped launches)
+constexpr int kFirstEpiThread = 11 * 32;
 
 struct SmemLayout {
-  uint32_t w, x, xch, bars, misc, total;
+  uint32_t w, x, xch, ucache, bars, misc, total;
 };
-template <int FMT, int NMMA>
-__host__ __device__ constexpr SmemLayout smem_layout(int stages) {
+__host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a_stages, int sw, int sx) {
   SmemLayout l{};
   l.w = 0;
-  l.x = l.w + stages * w_stage_bytes<FMT>();
-  l.xch = l.x + stages * TcCfg<NMMA>::X_STAGE;
-  l.bars = l.xch + kXchBytes;
-  // w_full, x_full, w_empty, x_empty [stages]; a_full, a_empty [A]; d_full, d_empty [2]; done
-  l.misc = l.bars + 8 * (4 * stages + 2 * TcCfg<NMMA>::A_STAGES + 5);
+  l.x = l.w + sw * wsb;
+  l.xch = l.x + sx * x_stage;
+  l.ucache = l.xch + kXchBytes;
+  l.bars = l.ucache + kUnitCacheBytes;
+  // w_full, w_empty [sw]; x_full, x_empty [sx]; a_full, a_empty [A]; d_full, d_empty [2]; done
+  l.misc = l.bars + 8 * (2 * sw + 2 * sx + 2 * a_stages + 5);
   l.total = l.misc + 16 + 1024;           // + slack to align the base to 1024 B
   return l;
 }
@@ -100,49 +105,69 @@ KL_DEVICE bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
 
 KL_DEVICE void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Unit bookkeeping shared by all roles.
+// Which problem a global unit belongs to, and where it sits in that problem.
 struct UnitInfo {
-  int tile, kb;
+  int prob, tile, kb, kb_total;
+  long long tile_u0;                  // global unit index of (prob, tile, kb = 0)
   bool seg_start, seg_end;
 };
-KL_DEVICE UnitInfo unit_info(long long u, long long u_lo, long long u_hi, int kb_total) {
-  UnitInfo r;
-  r.tile = static_cast<int>(u / kb_total);
-  r.kb = static_cast<int>(u % kb_total);
-  r.seg_start = (u == u_lo) || (r.kb == 0);
-  r.seg_end = (u == u_hi - 1) || (r.kb == kb_total - 1);
-  return r;
-}
+
+struct Problems {
+  const TcParams* p;
+  const long long* ucache;            // smem copy of unit_begin (count > 1)
+  KL_DEVICE const TcProblem& get(int i) const { return p->count == 1 ? p->single : p->table[i]; }
+  KL_DEVICE int find(long long u) const {
+    if (p->count == 1) return 0;
+    int lo = 0, hi = p->count - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (ucache[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
+  KL_DEVICE UnitInfo info(long long u, long long u_lo, long long u_hi) const {
+    UnitInfo r;
+    r.prob = find(u);
+    const TcProblem& pr = get(r.prob);
+    const long long rel = u - pr.unit_begin;
+    r.kb_total = pr.kb_total;
+    r.tile = static_cast<int>(rel / pr.kb_total);
+    r.kb = static_cast<int>(rel % pr.kb_total);
+    r.tile_u0 = u - r.kb;
+    r.seg_start = (u == u_lo) || (r.kb == 0);
+    r.seg_end = (u == u_hi - 1) || (r.kb == pr.kb_total - 1);
+    return r;
+  }
+};
 
 template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
 struct Epi {
   // Physical weight row of tile row r (0..127) of n-tile nt.
-  KL_DEVICE static int phys_row(const TcParams& p, int nt, int r) {
-    if constexpr (SWIGLU) return r < 64 ? nt * 64 + r : p.n_out + nt * 64 + (r - 64);
+  KL_DEVICE static int phys_row(const TcProblem& pr, int nt, int r) {
+    if constexpr (SWIGLU) return r < 64 ? nt * 64 + r : pr.n_out + nt * 64 + (r - 64);
     else return nt * 128 + r;
   }
-  KL_DEVICE static float row_scale(const TcParams& p, int prow) {
+  KL_DEVICE static float row_scale(const TcProblem& pr, int prow) {
     if constexpr (FMT == KL_W8_ROW) {
-      const int pr = prow < p.n ? prow : p.n - 1;
-      return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[pr]);
+      const int r = prow < pr.n ? prow : pr.n - 1;
+      return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[r]);
     } else {
       return 1.0f;
     }
   }
   // Emit 16 token columns [cb*16, cb*16+16) of tile row r.
-  KL_DEVICE static void emit16(const TcParams& p, int mt, int nt, int r, int cb, const float (&v)[16],
-                               float* xch) {
+  KL_DEVICE static void emit16(const TcProblem& pr, int mt, int nt, int r, int cb, const float (&v)[16], float* xch) {
     const int m0 = mt * NMMA + cb * 16;
     if constexpr (!SWIGLU) {
       const int n = nt * 128 + r;
-      if (n < p.n_out) {
+      if (n < pr.n_out) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = m0 + j;
-          if (m < p.m) {
-            const long long yi = p.y_transposed ? static_cast<long long>(n) * p.ldy + m
-                                                : static_cast<long long>(m) * p.ldy + n;
-            store_act<XBF16>(p.y, yi, v[j]);
+          if (m < pr.m) {
+            const long long yi = pr.y_transposed ? static_cast<long long>(n) * pr.ldy + m
+                                                 : static_cast<long long>(m) * pr.ldy + n;
+            store_act<XBF16>(pr.y, yi, v[j]);
           }
         }
       }
@@ -154,15 +179,15 @@ struct Epi {
       named_bar_epi();
       if (r < 64) {
         const int n = nt * 64 + r;
-        if (n < p.n_out) {
+        if (n < pr.n_out) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + j;
-            if (m < p.m) {
+            if (m < pr.m) {
               const float up = xch[r * 16 + ((j + r + 64) & 15)];
-              const long long yi = p.y_transposed ? static_cast<long long>(n) * p.ldy + m
-                                                  : static_cast<long long>(m) * p.ldy + n;
-              store_act<XBF16>(p.y, yi, swiglu_model_ordered<XBF16>(v[j], up));
+              const long long yi = pr.y_transposed ? static_cast<long long>(n) * pr.ldy + m
+                                                   : static_cast<long long>(m) * pr.ldy + n;
+              store_act<XBF16>(pr.y, yi, swiglu_model_ordered<XBF16>(v[j], up));
             }
           }
         }
@@ -174,56 +199,71 @@ struct Epi {
 
 template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
 __global__ void __launch_bounds__(kTcThreads, 1)
-tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
+tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   using Cfg = TcCfg<NMMA>;
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
   constexpr int WSB = w_stage_bytes<FMT>();
   constexpr int ROW_BYTES = is_w4<FMT>() ? 64 : 128;     // bytes of one tile row per stage
+  constexpr int A = Cfg::A_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemLayout L = smem_layout<FMT, NMMA>(stages);
+  const int SW = p.w_stages, SX = p.x_stages;
+  const SmemLayout L = smem_layout(WSB, Cfg::X_STAGE, A, SW, SX);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t s_w = s_base + L.w, s_x = s_base + L.x, s_bars = s_base + L.bars;
   float* xch = reinterpret_cast<float*>(smem + L.xch);
+  long long* ucache = reinterpret_cast<long long*>(smem + L.ucache);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc + 4);
   volatile int* fix_flag = reinterpret_cast<volatile int*>(smem + L.misc + 8);
-  const int S = stages;
   auto w_full = [&](int i) { return s_bars + 8u * i; };
-  auto x_full = [&](int i) { return s_bars + 8u * (S + i); };
-  auto w_empty = [&](int i) { return s_bars + 8u * (2 * S + i); };
-  auto x_empty = [&](int i) { return s_bars + 8u * (3 * S + i); };
-  auto a_full = [&](int i) { return s_bars + 8u * (4 * S + i); };
-  auto a_empty = [&](int i) { return s_bars + 8u * (4 * S + Cfg::A_STAGES + i); };
-  auto d_full = [&](int i) { return s_bars + 8u * (4 * S + 2 * Cfg::A_STAGES + i); };
-  auto d_empty = [&](int i) { return s_bars + 8u * (4 * S + 2 * Cfg::A_STAGES + 2 + i); };
-  const uint32_t done_bar = s_bars + 8u * (4 * S + 2 * Cfg::A_STAGES + 4);
+  auto w_empty = [&](int i) { return s_bars + 8u * (SW + i); };
+  auto x_full = [&](int i) { return s_bars + 8u * (2 * SW + i); };
+  auto x_empty = [&](int i) { return s_bars + 8u * (2 * SW + SX + i); };
+  auto a_full = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + i); };
+  auto a_empty = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + A + i); };
+  auto d_full = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + 2 * A + i); };
+  auto d_empty = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + 2 * A + 2 + i); };
+  const uint32_t done_bar = s_bars + 8u * (2 * SW + 2 * SX + 2 * A + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long G = gridDim.x, c = blockIdx.x;
   const long long u_lo = unit_lo(c, p.units, G), u_hi = unit_lo(c + 1, p.units, G);
   const int n_local = static_cast<int>(u_hi - u_lo);
-  const int KB = p.kb_total;
+  Problems probs{&p, ucache};
 
+  if (p.count > 1) {
+    for (int i = threadIdx.x; i < p.count; i += blockDim.x) ucache[i] = p.table[i].unit_begin;
+    __syncthreads();                        // unit cache visible before any unit decoding
+  }
+  // Thread 0 initialises the barriers and starts streaming weights at once
+  // (before TMEM allocation and the block-wide barrier): weights are static, so
+  // this also runs ahead of the previous kernel in the stream (PDL).
+  Pipe pw{0, SW, 0};
+  int w_pre = 0;
+  auto issue_w = [&](int i) {
+    const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
+    const TcProblem& pr = probs.get(ui.prob);
+    const int nt = ui.tile % pr.n_tiles;
+    const uint32_t dst = s_w + pw.idx * WSB;
+    mbar_arrive_expect_tx(w_full(pw.idx), WSB);
+    const int y0 = SWIGLU ? nt * 64 : nt * 128;
+    const int y1 = SWIGLU ? pr.n_out + nt * 64 : nt * 128 + 64;
+    tma_load_2d(dst, &pr.tmap_w, ui.kb * ROW_BYTES, y0, w_full(pw.idx));
+    tma_load_2d(dst + WSB / 2, &pr.tmap_w, ui.kb * ROW_BYTES, y1, w_full(pw.idx));
+  };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(w_full(i), 1);
-      mbar_init(x_full(i), 1);
-      mbar_init(w_empty(i), 4);
-      mbar_init(x_empty(i), 1);
-    }
-    for (int i = 0; i < Cfg::A_STAGES; ++i) {
-      mbar_init(a_full(i), 4);
-      mbar_init(a_empty(i), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(d_full(i), 1);
-      mbar_init(d_empty(i), 4);
-    }
+    for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), 8); }
+    for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), 1); }
+    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), 8); mbar_init(a_empty(i), 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), 1); mbar_init(d_empty(i), 4); }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     *fix_flag = 0;
     fence_mbar_init();
+    if (n_local > 0) prefetch_tmap(&probs.get(probs.find(u_lo)).tmap_w);
+    w_pre = n_local < SW ? n_local : SW;
+    for (int i = 0; i < w_pre; ++i) { issue_w(i); pw.next(); }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_holder), Cfg::TMEM_COLS);
@@ -236,56 +276,50 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
   pdl_launch_dependents();
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ W producer
     if (lane == 0) {
-      prefetch_tmap(&p.tmap_w);
-      prefetch_tmap(&p.tmap_x);
-      Pipe pw{0, S, 0}, px{0, S, 0};
       bool ok = true;
-      bool issued_w[8] = {}, issued_x[8] = {};
-      uint32_t last_w[8] = {}, last_x[8] = {};
-      auto issue_w = [&](int i) {
-        issued_w[pw.idx] = true;
-        last_w[pw.idx] = pw.phase;
-        const UnitInfo ui = unit_info(u_lo + i, u_lo, u_hi, KB);
-        const int nt = ui.tile % p.n_tiles;
-        const uint32_t dst = s_w + pw.idx * WSB;
-        mbar_arrive_expect_tx(w_full(pw.idx), WSB);
-        const int y0 = SWIGLU ? nt * 64 : nt * 128;
-        const int y1 = SWIGLU ? p.n_out + nt * 64 : nt * 128 + 64;
-        tma_load_2d(dst, &p.tmap_w, ui.kb * ROW_BYTES, y0, w_full(pw.idx));
-        tma_load_2d(dst + WSB / 2, &p.tmap_w, ui.kb * ROW_BYTES, y1, w_full(pw.idx));
-      };
-      auto issue_x = [&](int i) {
-        issued_x[px.idx] = true;
-        last_x[px.idx] = px.phase;
-        const UnitInfo ui = unit_info(u_lo + i, u_lo, u_hi, KB);
-        const int mt = ui.tile / p.n_tiles;
+      int last_prob = -1;
+      for (int i = w_pre; i < n_local; ++i) {
+        if (!(ok = wait_bar(w_empty(pw.idx), pw.phase ^ 1u, abort_flag, p.status))) break;
+        if (p.count > 1) {
+          const int pi = probs.find(u_lo + i);
+          if (pi != last_prob) { prefetch_tmap(&probs.get(pi).tmap_w); last_prob = pi; }
+        }
+        issue_w(i);
+        pw.next();
+      }
+      if (!ok) {
+        // Abort path: let every weight copy already issued land before smem is released.
+        for (int s = 0; s < SW; ++s) {
+          mbar_wait_time(w_full(s), 0);
+          mbar_wait_time(w_full(s), 1);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ X producer
+    if (lane == 0) {
+      pdl_wait();                          // activations come from the previous kernel
+      Pipe px{0, SX, 0};
+      bool ok = true;
+      int last_prob = -1;
+      for (int i = 0; i < n_local; ++i) {
+        if (!(ok = wait_bar(x_empty(px.idx), px.phase ^ 1u, abort_flag, p.status))) break;
+        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
+        const TcProblem& pr = probs.get(ui.prob);
+        if (ui.prob != last_prob) { prefetch_tmap(&pr.tmap_x); last_prob = ui.prob; }
+        const int mt = ui.tile / pr.n_tiles;
         const uint32_t dst = s_x + px.idx * Cfg::X_STAGE;
         mbar_arrive_expect_tx(x_full(px.idx), Cfg::X_STAGE);
-        tma_load_2d(dst, &p.tmap_x, ui.kb * kTcKBlock, mt * NMMA, x_full(px.idx));
-        tma_load_2d(dst + Cfg::X_ATOM, &p.tmap_x, ui.kb * kTcKBlock + 64, mt * NMMA, x_full(px.idx));
-      };
-      const int pre = n_local < S ? n_local : S;
-      // Weights are static: stream the first stages before waiting on the
-      // previous kernel in the stream (programmatic dependent launch).
-      for (int i = 0; i < pre; ++i) { issue_w(i); pw.next(); }
-      pdl_wait();
-      for (int i = 0; i < n_local && ok; ++i) {
-        if (i >= pre) {
-          if (!(ok = wait_bar(w_empty(pw.idx), pw.phase ^ 1u, abort_flag, p.status))) break;
-          issue_w(i);
-          pw.next();
-        }
-        if (!(ok = wait_bar(x_empty(px.idx), px.phase ^ 1u, abort_flag, p.status))) break;
-        issue_x(i);
+        tma_load_2d(dst, &pr.tmap_x, ui.kb * kTcKBlock, mt * NMMA, x_full(px.idx));
+        tma_load_2d(dst + Cfg::X_ATOM, &pr.tmap_x, ui.kb * kTcKBlock + 64, mt * NMMA, x_full(px.idx));
         px.next();
       }
       if (!ok) {
-        // Abort path: let every copy already issued land before smem is released.
-        for (int s = 0; s < S; ++s) {
-          if (issued_w[s]) mbar_wait_time(w_full(s), last_w[s]);
-          if (issued_x[s]) mbar_wait_time(x_full(s), last_x[s]);
+        for (int s = 0; s < SX; ++s) {
+          mbar_wait_time(x_full(s), 0);
+          mbar_wait_time(x_full(s), 1);
         }
       }
     }
@@ -293,10 +327,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
-      Pipe px{0, S, 0}, pa{0, Cfg::A_STAGES, 0}, pd{0, 2, 0};
+      Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
       bool ok = true;
       for (int i = 0; i < n_local && ok; ++i) {
-        const UnitInfo ui = unit_info(u_lo + i, u_lo, u_hi, KB);
+        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
         const bool chunk_start = grouped<FMT>() ? true : ui.seg_start;
         const bool chunk_end = grouped<FMT>() ? true : ui.seg_end;
         if (chunk_start && !(ok = wait_bar(d_empty(pd.idx), pd.phase ^ 1u, abort_flag, p.status))) break;
@@ -324,22 +358,23 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
       tc_commit(done_bar);
       mbar_wait_time(done_bar, 0);
     }
-  } else if (warp < 6) {
+  } else if (warp < 11) {
     // -------------------------------------------------------------- converters
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
+    const int h = (warp - 3) >> 2;          // which half of the K block (64 elements)
     const int r = q * 32 + lane;            // tile row owned by this thread
-    Pipe pw{0, S, 0}, pa{0, Cfg::A_STAGES, 0};
+    Pipe pwc{0, SW, 0}, pa{0, A, 0};
     for (int i = 0; i < n_local; ++i) {
-      const UnitInfo ui = unit_info(u_lo + i, u_lo, u_hi, KB);
-      if (!wait_bar(w_full(pw.idx), pw.phase, abort_flag, p.status)) break;
+      if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
-      const uint8_t* wrow = smem + L.w + pw.idx * WSB + r * ROW_BYTES;
-      uint32_t out[64];
+      const uint8_t* wrow = smem + L.w + pwc.idx * WSB + r * ROW_BYTES;
+      uint32_t out[32];
       if constexpr (!is_w4<FMT>()) {
-        // 128 int8 = 8 chunks of 16 B; 128B swizzle: chunk c at c ^ (r & 7)
+        // 64 int8 = 4 chunks of 16 B; 128B swizzle: chunk c at c ^ (r & 7)
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((cc ^ (r & 7)) << 4));
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk = 4 * h + cc;
+          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((chunk ^ (r & 7)) << 4));
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
@@ -348,20 +383,23 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
           }
         }
       } else {
-        // 128 nibbles = 4 chunks of 16 B; 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
-        const int nt = ui.tile % p.n_tiles;
-        int prow = E::phys_row(p, nt, r);
-        prow = prow < p.n ? prow : p.n - 1;
+        // 64 nibbles = 2 chunks of 16 B; 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
+        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
+        const TcProblem& pr = probs.get(ui.prob);
+        const int nt = ui.tile % pr.n_tiles;
+        int prow = E::phys_row(pr, nt, r);
+        prow = prow < pr.n ? prow : pr.n - 1;
         float z = 8.0f;
         if constexpr (FMT == KL_W4_ASYM)
-          z = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.zeros)[static_cast<long long>(prow) * KB + ui.kb]);
+          z = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.zeros)[static_cast<long long>(prow) * ui.kb_total + ui.kb]);
         const uint32_t bias = XBF16 ? pack_bf16x2(-(128.0f + z), -(128.0f + z))
                                     : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
                                          : (FMT == KL_W4_SYM ? 0x64086408u : 0x64006400u);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((cc ^ ((r >> 1) & 3)) << 4));
+        for (int cc = 0; cc < 2; ++cc) {
+          const int chunk = 2 * h + cc;
+          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((chunk ^ ((r >> 1) & 3)) << 4));
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
@@ -374,9 +412,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
           }
         }
       }
-      const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + 64u * pa.idx;
+      const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + 64u * pa.idx + 32u * h;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 2; ++j) {
         uint32_t part[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) part[t] = out[16 * j + t];
@@ -387,9 +425,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(a_full(pa.idx));
-        mbar_arrive(w_empty(pw.idx));
+        mbar_arrive(w_empty(pwc.idx));
       }
-      pw.next();
+      pwc.next();
       pa.next();
     }
   } else {
@@ -401,10 +439,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
     float acc[grouped<FMT>() ? NMMA : 1];
     int seg_kb0 = 0;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const long long first_tile_u0 = n_local > 0 ? probs.info(u_lo, u_lo, u_hi).tile_u0 : 0;
     bool ok = true;
     for (int i = 0; i < n_local && ok; ++i) {
-      const UnitInfo ui = unit_info(u_lo + i, u_lo, u_hi, KB);
-      const int mt = ui.tile / p.n_tiles, nt = ui.tile % p.n_tiles;
+      const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
+      const TcProblem& pr = probs.get(ui.prob);
+      const int mt = ui.tile / pr.n_tiles, nt = ui.tile % pr.n_tiles;
       if (ui.seg_start) {
         seg_kb0 = ui.kb;
         if constexpr (grouped<FMT>()) {
@@ -417,21 +457,20 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
       if (!(ok = wait_bar(d_full(pd.idx), pd.phase, abort_flag, p.status))) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + lane_base + Cfg::D_COL0 + pd.idx * Cfg::D_PITCH;
-      const int prow = E::phys_row(p, nt, r);
-      const bool full_tile = ui.seg_end && seg_kb0 == 0 && ui.kb == KB - 1;
+      const int prow = E::phys_row(pr, nt, r);
+      const bool full_tile = ui.seg_end && seg_kb0 == 0 && ui.kb == ui.kb_total - 1;
       float* part_base = nullptr;
       if (ui.seg_end && !full_tile) {
-        const long long first_tile = unit_lo(c, p.units, G) / KB;
-        const int slot = (ui.tile == first_tile) ? 0 : 1;
+        const int slot = (ui.tile_u0 == first_tile_u0) ? 0 : 1;
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
       }
       if constexpr (grouped<FMT>()) {
-        const int pr = prow < p.n ? prow : p.n - 1;
+        const int pr_row = prow < pr.n ? prow : pr.n - 1;
         float s;
         if constexpr (FMT == KL_W4_ASYM)
-          s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[static_cast<long long>(pr) * KB + ui.kb]);
+          s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ui.kb_total + ui.kb]);
         else
-          s = reinterpret_cast<const float*>(p.scales)[static_cast<long long>(pr) * KB + ui.kb];
+          s = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ui.kb_total + ui.kb];
 #pragma unroll
         for (int cb = 0; cb < NMMA / 16; ++cb) {
           uint32_t v[16];
@@ -451,7 +490,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = acc[cb * 16 + j];
-            E::emit16(p, mt, nt, r, cb, o, xch);
+            E::emit16(pr, mt, nt, r, cb, o, xch);
           }
           continue;
         }
@@ -460,7 +499,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
       } else {
-        const float s = E::row_scale(p, prow);
+        const float s = E::row_scale(pr, prow);
         for (int cb = 0; cb < NMMA / 16; ++cb) {
           uint32_t v[16];
           tmem_ld16(d_tmem + 16u * cb, v);
@@ -469,7 +508,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = __uint_as_float(v[j]) * s;
-            E::emit16(p, mt, nt, r, cb, o, xch);
+            E::emit16(pr, mt, nt, r, cb, o, xch);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = __uint_as_float(v[j]);
@@ -482,12 +521,11 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
         if (full_tile) continue;
       }
       // ---- split tile: publish the partial, the last contributor finishes it.
-      const long long t_first_unit = static_cast<long long>(ui.tile) * KB;
-      const long long c_first = unit_owner(t_first_unit, p.units, G);
-      const long long c_last = unit_owner(t_first_unit + KB - 1, p.units, G);
+      const long long c_first = unit_owner(ui.tile_u0, p.units, G);
+      const long long c_last = unit_owner(ui.tile_u0 + ui.kb_total - 1, p.units, G);
       __threadfence();
       named_bar_epi();
-      if (threadIdx.x == 6 * 32) {
+      if (threadIdx.x == kFirstEpiThread) {
         const int old = atomicAdd(p.counters + c_first, 1);
         const int last = (old == static_cast<int>(c_last - c_first));
         if (last) p.counters[c_first] = 0;   // ready for the next launch
@@ -498,21 +536,25 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p, const int stages) {
       named_bar_epi();                        // everyone read fix_flag before it is reused
       if (!last) continue;
       __threadfence();
-      const float s = grouped<FMT>() ? 1.0f : E::row_scale(p, prow);
+      const float s = grouped<FMT>() ? 1.0f : E::row_scale(pr, prow);
       for (int cb = 0; cb < NMMA / 16; ++cb) {
         float o[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = 0.f;
+#pragma unroll 4
         for (long long cc = c_first; cc <= c_last; ++cc) {
-          const long long ft = unit_lo(cc, p.units, G) / KB;
-          const int sl = (ui.tile == ft) ? 0 : 1;
-          const float* src = p.partials + (cc * 2 + sl) * static_cast<long long>(NMMA) * 128;
+          // slot 0 holds a contributor's first tile: the one its range starts in
+          const int sl = unit_lo(cc, p.units, G) >= ui.tile_u0 ? 0 : 1;
+          const float* src = p.partials + (cc * 2 + sl) * static_cast<long long>(NMMA) * 128 + cb * 16 * 128 + r;
+          float t[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] += __ldcg(src + (cb * 16 + j) * 128 + r);
+          for (int j = 0; j < 16; ++j) t[j] = __ldcg(src + j * 128);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] += t[j];
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] *= s;
-        E::emit16(p, mt, nt, r, cb, o, xch);
+        E::emit16(pr, mt, nt, r, cb, o, xch);
       }
     }
   }
@@ -548,7 +590,7 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, p, plan.stages);
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int FMT, bool SWIGLU, bool XBF16>
@@ -573,40 +615,40 @@ cudaError_t launch_fmt(const TcParams& p, const TcPlan& plan, int fmt, bool pdl,
   }
 }
 
-int tc_stage_bytes(int fmt, int nmma) {
-  return ((fmt == KL_W4_SYM || fmt == KL_W4_ASYM) ? 8192 : 16384) + 2 * nmma * 128;
-}
-int tc_fixed_bytes(int nmma) {
-  const int a = nmma == 128 ? 4 : (nmma == 64 ? 2 : 3);
-  return kXchBytes + 8 * (2 * a + 5) + 16 + 1024;
-}
-
 }  // namespace
 
-TcPlan plan_tc(int m, int n, int k, int fmt, bool swiglu, int sm_count) {
+int tc_choose_nmma(int m, int fmt) {
+  const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
+  const int n = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+  return (w4 && n > 64) ? 64 : n;     // group mode: the host splits M into 64-token launches
+}
+
+long long tc_problem_tiles(TcProblem& pr, int n_mma, bool swiglu) {
+  pr.m_tiles = (pr.m + n_mma - 1) / n_mma;
+  pr.n_tiles = swiglu ? (pr.n_out + 63) / 64 : (pr.n + 127) / 128;
+  pr.kb_total = (pr.k + kTcKBlock - 1) / kTcKBlock;
+  return static_cast<long long>(pr.m_tiles) * pr.n_tiles * pr.kb_total;
+}
+
+TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count) {
   TcPlan t{};
   t.ok = false;
+  if (units <= 0 || sm_count <= 0) return t;
   const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
-  if (!(fmt == KL_W8_ROW || w4)) return t;
-  if (m <= 0 || n <= 0 || k <= 0) return t;
-  if (swiglu && (n % 2)) return t;
-  t.n_mma = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
-  if (w4 && t.n_mma > 64) t.n_mma = 64;      // group mode: host splits M into 64-token launches
-  const int n_out = swiglu ? n / 2 : n;
-  t.m_tiles = (m + t.n_mma - 1) / t.n_mma;
-  if (w4) t.m_tiles = 1;
-  t.n_tiles = swiglu ? (n_out + 63) / 64 : (n + 127) / 128;
-  t.kb_total = (k + kTcKBlock - 1) / kTcKBlock;
-  t.units = static_cast<long long>(t.m_tiles) * t.n_tiles * t.kb_total;
-  t.grid = static_cast<int>(std::min<long long>(t.units, sm_count));
-  const int per_stage = tc_stage_bytes(fmt, t.n_mma);
-  const int budget = (t.n_mma == 128 ? 200 : 104) * 1024 - tc_fixed_bytes(t.n_mma);
-  t.stages = std::max(2, std::min(6, budget / per_stage));
-  t.a_stages = t.n_mma == 128 ? 4 : (t.n_mma == 64 ? 2 : 3);
-  t.smem = t.stages * per_stage + tc_fixed_bytes(t.n_mma) + 8 * 4 * t.stages;
-  t.tmem_cols = t.n_mma == 128 ? 512 : 256;
-  t.workspace = kCounterBytes + static_cast<size_t>(t.grid) * 2 * t.n_mma * 128 * sizeof(float);
-  if (t.grid > kCounterBytes / 4) return t;
+  t.n_mma = n_mma;
+  t.units = units;
+  t.grid = static_cast<int>(std::min<long long>(units, sm_count));
+  const int wsb = w4 ? 8192 : 16384;
+  const int x_stage = 2 * n_mma * 128;
+  const int a_stages = n_mma == 128 ? 4 : 6;
+  t.x_stages = n_mma == 128 ? 3 : 4;
+  const int budget = 220 * 1024;
+  int sw = kMaxWStages;
+  while (sw > 2 && static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total) > budget) --sw;
+  t.w_stages = sw;
+  t.smem = static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total);
+  t.workspace = kCounterBytes + static_cast<size_t>(t.grid) * 2 * n_mma * 128 * sizeof(float);
+  if (t.grid > kCounterBytes / 4 || t.smem > 227 * 1024) return t;
   t.ok = true;
   return t;
 }

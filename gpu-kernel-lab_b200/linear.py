@@ -145,3 +145,63 @@ class QuantLinear(nn.Module):
 
     def extra_repr(self):
         return f"in_features={self.in_features}, out_features={self.out_features}, format={self.format}, swiglu={self.swiglu}"
+
+
+class GroupedLinear:
+    """Many independent quantized linears run by ONE persistent tcgen05 launch.
+
+    ``GroupedLinear([(x0, w0, y0), (x1, w1, y1), ...])`` fixes the buffers (the
+    problem table holds TMA descriptors of these exact tensors) and ``run()``
+    computes every ``y_i = x_i @ dequant(w_i)^T`` with a single kernel that
+    streams the weights of all problems through one stream-K partition -- no
+    launch gaps between problems.  All weights share one format (KL_W8_ROW or
+    a group-128 4-bit format); SwiGLU applies to all problems or none.
+    Capture ``run()`` in a CUDA graph for repeated use.
+    """
+
+    def __init__(self, problems, *, swiglu: bool = False):
+        import ctypes
+        if not problems:
+            raise ValueError("at least one problem required")
+        specs = [weight_spec(w) for _, w, _ in problems]
+        fmt = specs[0][0]
+        if any(s[0] != fmt for s in specs):
+            raise ValueError("all problems must share one weight format")
+        x0 = problems[0][0]
+        self.device = x0.device
+        self.problems = problems              # keep the tensors alive
+        arr = (N.KlProblem * len(problems))()
+        for i, ((x, w, y), spec) in enumerate(zip(problems, specs)):
+            _, data, scales, zeros, _inv, n, k, group = spec
+            m = x.numel() // k
+            n_out = n // 2 if swiglu else n
+            if x.dtype != x0.dtype or not x.is_contiguous() or x.device != self.device or x.shape[-1] != k:
+                raise ValueError(f"problem {i}: x must be contiguous [.., {k}] {x0.dtype} on {self.device}")
+            if y.dtype != x.dtype or not y.is_contiguous() or y.numel() != m * n_out:
+                raise ValueError(f"problem {i}: y must be contiguous with {m}x{n_out} elements")
+            arr[i] = N.KlProblem(x.data_ptr(), data.data_ptr(), scales.data_ptr(),
+                                 zeros.data_ptr() if zeros is not None else None, y.data_ptr(), m, n, k, group)
+        lib = N.lib()
+        nbytes = lib.kl_grouped_table_bytes(len(problems))
+        if nbytes == 0:
+            raise ValueError("too many problems for one grouped launch")
+        self._host = (ctypes.c_uint8 * nbytes)()
+        N.check(lib.kl_grouped_encode(arr, len(problems), N.act_dtype_code(x0.dtype), fmt, int(swiglu),
+                                      self._host, nbytes))
+        host_t = torch.frombuffer(self._host, dtype=torch.uint8)
+        self._device = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.device)
+        off = (-self._device.data_ptr()) % 256
+        self._dev_view = self._device[off:off + nbytes]
+        self._dev_view.copy_(host_t)
+        with torch.cuda.device(self.device):
+            self._ws_bytes = lib.kl_grouped_workspace_bytes(self._host)
+            N.workspace(self.device, self._ws_bytes)
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def run(self, *, pdl: bool = False, workspace: torch.Tensor | None = None):
+        lib = N.lib()
+        ws = workspace if workspace is not None else N.workspace(self.device, self._ws_bytes)
+        with torch.cuda.device(self.device):
+            N.check(lib.kl_linear_grouped(self._host, N.ptr(self._dev_view), N.ptr(ws),
+                                          ws.numel() * ws.element_size(), N.KL_FLAG_PDL if pdl else 0,
+                                          N.stream_handle(self.device)))

@@ -87,6 +87,34 @@ int kl_linear(const void* x, int x_dtype, int m, int k,
 size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, int flags);
 
 /*
+ * Grouped launch: many independent GEMMs (same weight format, activation dtype
+ * and SwiGLU mode; any shapes) streamed by ONE persistent tcgen05 kernel --
+ * no launch gaps, one stream-K partition over the weights of every problem.
+ * No reference counterpart: it runs the BASELINE.json config 1 projection
+ * set (independent activations per GEMM) as a single unit of work.
+ *   1. kl_grouped_encode() builds the problem table in HOST memory
+ *      (kl_grouped_table_bytes(count) bytes; TMA descriptors included);
+ *   2. the caller copies it to a 64-byte-aligned DEVICE buffer;
+ *   3. kl_linear_grouped() launches (both copies are passed: the host copy
+ *      for the launch geometry, the device copy for the kernel).
+ * Every x / y / w pointer stays fixed for the life of the table.
+ */
+typedef struct kl_problem {
+  const void* x;        /* [m, k] activations                       */
+  const void* w;        /* weights in the group's w_format          */
+  const void* scales;
+  const void* zeros;    /* KL_W4_ASYM only                          */
+  void* y;              /* [m, n] or [m, n/2] with swiglu           */
+  int m, n, k, group;   /* group: 128 for the 4-bit formats         */
+} kl_problem;
+size_t kl_grouped_table_bytes(int count);
+int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_format, int swiglu,
+                      void* host_table, size_t table_bytes);
+size_t kl_grouped_workspace_bytes(const void* host_table);
+int kl_linear_grouped(const void* host_table, const void* device_table, void* workspace,
+                      size_t workspace_bytes, int flags, void* stream);
+
+/*
  * The reference's op, same arguments and checks (warp_gemv.cu:56-72):
  *   x bf16 [K]; w int8 [N,K] (w_is_int8 = 1, with f32 scales [N,K/group] and
  *   f32 inverse [K]) or bf16 [N,K] (w_is_int8 = 0, scales/inverse ignored);

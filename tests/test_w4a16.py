@@ -90,3 +90,18 @@ def test_w4_f16_activations():
     assert y.dtype == torch.float16
     err = np.abs(y.float().cpu().numpy() - ref)
     assert err.max() <= 2e-2 and np.linalg.norm(y.float().cpu().numpy() - ref) / np.linalg.norm(ref) <= 5e-3
+
+
+@pytest.mark.parametrize("m", [1, 16])
+def test_w4_grouped(m):
+    probs, refs = [], []
+    for i, (name, (n, k)) in enumerate(QWEN.items()):
+        x, w = make(m, n, k, seed=50 + i)
+        p, d, s, z = quantize_asym(w)
+        probs.append((x.cuda(), p, torch.empty(m, n, device="cuda", dtype=torch.bfloat16)))
+        rows = np.sort(np.random.default_rng(i).choice(n, min(n, 512), replace=False))
+        refs.append((rows, O.linear_f32(x.float().numpy(), O.dequantize_int4_asym(d[rows], s[rows], z[rows], 128))))
+    kl.GroupedLinear(probs).run()
+    torch.cuda.synchronize()
+    for (_, p, y), (rows, ref) in zip(probs, refs):
+        assert_matches_oracle(y[:, torch.from_numpy(rows).cuda()], ref, what=f"w4 grouped m={m}")
