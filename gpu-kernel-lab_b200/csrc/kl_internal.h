@@ -33,8 +33,7 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& p, int fmt, bool swig
 // (n_mma tokens per tile) TMA-staged in shared memory as the B operand.
 constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
 constexpr int kTcKBlock = 128;        // K elements per pipeline stage
-constexpr int kTcWarps = 15;          // W-TMA, MMA, X-TMA, 8 converter, 4 epilogue warps
-constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kTcWarps = 15;          // W-TMA, MMA, X-TMA, 8 converter, 4 epilogue warps (+ extra MMA issuers)
 constexpr int kCounterBytes = 64 * 1024;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxGroup = 512;        // problems per grouped launch
@@ -72,6 +71,7 @@ struct TcPlan {
   size_t workspace;                   // counters + partials
 };
 int tc_choose_nmma(int m, int fmt);
+int tc_threads(int n_mma);           // block size of the tcgen05 kernel for this token tile
 // Fill the tiling fields of a problem (m_tiles, n_tiles, kb_total); returns its unit count.
 long long tc_problem_tiles(TcProblem& pr, int n_mma, bool swiglu);
 TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count);

@@ -44,13 +44,22 @@ namespace kl {
 
 namespace {
 
+// A single thread issues one small-N tcgen05.mma every ~27 ns regardless of
+// its size, so at decode shapes the MMA issue rate -- not the tensor core --
+// bounds the weight stream.  Each K block's 8 MMAs are therefore split across
+// NI issuing threads (separate warps), each accumulating into its own TMEM
+// region; the epilogue adds the NI partial accumulators.
 template <int NMMA>
 struct TcCfg {
-  static constexpr int A_STAGES = NMMA == 128 ? 4 : 6;
-  static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D buffer
+  static constexpr int NI = NMMA <= 32 ? 4 : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
+  static constexpr int THREADS = (kTcWarps + NI - 1) * 32;
+  static constexpr int A_STAGES = 4;
+  static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D accumulator
   static constexpr int D_COL0 = 64 * A_STAGES;               // A stages first (64 cols each)
   static constexpr int TMEM_COLS = 512;
-  static_assert(D_COL0 + 2 * D_PITCH <= TMEM_COLS, "TMEM budget");
+  static_assert(D_COL0 + 2 * NI * D_PITCH <= TMEM_COLS, "TMEM budget");
+  // D accumulator of buffer b (0/1) and issuer w
+  static constexpr uint32_t d_col(int b, int w) { return D_COL0 + (b * NI + w) * D_PITCH; }
   static constexpr int X_ATOM = NMMA * 128;                  // bytes: NMMA rows x 64 bf16
   static constexpr int X_STAGE = 2 * X_ATOM;
 };
@@ -103,14 +112,19 @@ KL_DEVICE bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
   }
 }
 
-KL_DEVICE void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Abort path of a TMA producer: wait (time-bounded) until the last copy issued
+// into every stage of a ring has landed, so no copy is in flight when the
+// CTA's shared memory is released.  Stage s was last filled by issue number
+// s + n*((issued-1-s)/n), whose barrier phase parity is ((that)/n) & 1.
+template <typename BarFn>
+KL_DEVICE void drain_ring(BarFn full, int n, int issued) {
+  for (int s = 0; s < n && s < issued; ++s) {
+    const int last = s + n * ((issued - 1 - s) / n);
+    mbar_wait_time(full(s), static_cast<uint32_t>((last / n) & 1));
+  }
+}
 
-// Which problem a global unit belongs to, and where it sits in that problem.
-struct UnitInfo {
-  int prob, tile, kb, kb_total;
-  long long tile_u0;                  // global unit index of (prob, tile, kb = 0)
-  bool seg_start, seg_end;
-};
+KL_DEVICE void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct Problems {
   const TcParams* p;
@@ -125,18 +139,56 @@ struct Problems {
     }
     return lo;
   }
-  KL_DEVICE UnitInfo info(long long u, long long u_lo, long long u_hi) const {
-    UnitInfo r;
-    r.prob = find(u);
-    const TcProblem& pr = get(r.prob);
-    const long long rel = u - pr.unit_begin;
-    r.kb_total = pr.kb_total;
-    r.tile = static_cast<int>(rel / pr.kb_total);
-    r.kb = static_cast<int>(rel % pr.kb_total);
-    r.tile_u0 = u - r.kb;
-    r.seg_start = (u == u_lo) || (r.kb == 0);
-    r.seg_end = (u == u_hi - 1) || (r.kb == pr.kb_total - 1);
-    return r;
+};
+
+// Walks a CTA's contiguous range of (problem, m-tile, n-tile, k-block) units
+// incrementally: one division at start-up, none per unit (64-bit division is
+// a long instruction sequence on the GPU and sat on every role's critical path).
+struct Cursor {
+  const Problems* ps;
+  const TcProblem* pr;
+  long long u, u_lo, u_hi, tile_u0;
+  int prob, mt, nt, kb, kb_total, n_tiles, m_tiles;
+  KL_DEVICE void load() {
+    pr = &ps->get(prob);
+    kb_total = pr->kb_total;
+    n_tiles = pr->n_tiles;
+    m_tiles = pr->m_tiles;
+  }
+  KL_DEVICE void init(const Problems& P, long long lo, long long hi) {
+    ps = &P;
+    u_lo = lo;
+    u_hi = hi;
+    u = lo;
+    prob = 0;
+    mt = nt = kb = 0;
+    tile_u0 = lo;
+    if (lo >= hi) return;
+    prob = P.find(lo);
+    load();
+    const int rel = static_cast<int>(lo - pr->unit_begin);   // < 2^31 units per problem
+    const int tile = rel / kb_total;
+    kb = rel - tile * kb_total;
+    mt = tile / n_tiles;
+    nt = tile - mt * n_tiles;
+    tile_u0 = lo - kb;
+  }
+  KL_DEVICE bool seg_start() const { return u == u_lo || kb == 0; }
+  KL_DEVICE bool seg_end() const { return u == u_hi - 1 || kb == kb_total - 1; }
+  KL_DEVICE void next() {
+    ++u;
+    if (++kb == kb_total) {
+      kb = 0;
+      tile_u0 = u;
+      if (++nt == n_tiles) {
+        nt = 0;
+        if (++mt == m_tiles) {
+          mt = 0;
+          ++prob;
+          if (u < u_hi) load();
+        }
+      }
+    }
   }
 };
 
@@ -198,7 +250,7 @@ struct Epi {
 };
 
 template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfg<NMMA>::THREADS, 1)
 tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   using Cfg = TcCfg<NMMA>;
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
@@ -241,29 +293,30 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   // this also runs ahead of the previous kernel in the stream (PDL).
   Pipe pw{0, SW, 0};
   int w_pre = 0;
-  auto issue_w = [&](int i) {
-    const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
-    const TcProblem& pr = probs.get(ui.prob);
-    const int nt = ui.tile % pr.n_tiles;
+  Cursor cw;
+  auto issue_w = [&]() {
+    const TcProblem& pr = *cw.pr;
     const uint32_t dst = s_w + pw.idx * WSB;
     mbar_arrive_expect_tx(w_full(pw.idx), WSB);
-    const int y0 = SWIGLU ? nt * 64 : nt * 128;
-    const int y1 = SWIGLU ? pr.n_out + nt * 64 : nt * 128 + 64;
-    tma_load_2d(dst, &pr.tmap_w, ui.kb * ROW_BYTES, y0, w_full(pw.idx));
-    tma_load_2d(dst + WSB / 2, &pr.tmap_w, ui.kb * ROW_BYTES, y1, w_full(pw.idx));
+    const int y0 = SWIGLU ? cw.nt * 64 : cw.nt * 128;
+    const int y1 = SWIGLU ? pr.n_out + cw.nt * 64 : cw.nt * 128 + 64;
+    tma_load_2d(dst, &pr.tmap_w, cw.kb * ROW_BYTES, y0, w_full(pw.idx));
+    tma_load_2d(dst + WSB / 2, &pr.tmap_w, cw.kb * ROW_BYTES, y1, w_full(pw.idx));
+    cw.next();
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), 8); }
-    for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), 1); }
-    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), 8); mbar_init(a_empty(i), 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), 1); mbar_init(d_empty(i), 4); }
-    mbar_init(done_bar, 1);
+    for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), Cfg::NI); }
+    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), 8); mbar_init(a_empty(i), Cfg::NI); }
+    for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), Cfg::NI); mbar_init(d_empty(i), 4); }
+    mbar_init(done_bar, Cfg::NI);
     *abort_flag = 0;
     *fix_flag = 0;
     fence_mbar_init();
-    if (n_local > 0) prefetch_tmap(&probs.get(probs.find(u_lo)).tmap_w);
+    cw.init(probs, u_lo, u_hi);
+    if (n_local > 0) prefetch_tmap(&cw.pr->tmap_w);
     w_pre = n_local < SW ? n_local : SW;
-    for (int i = 0; i < w_pre; ++i) { issue_w(i); pw.next(); }
+    for (int i = 0; i < w_pre; ++i) { issue_w(); pw.next(); }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_holder), Cfg::TMEM_COLS);
@@ -279,23 +332,15 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     // ------------------------------------------------------------ W producer
     if (lane == 0) {
       bool ok = true;
-      int last_prob = -1;
+      int last_prob = cw.prob, issued = w_pre;
       for (int i = w_pre; i < n_local; ++i) {
         if (!(ok = wait_bar(w_empty(pw.idx), pw.phase ^ 1u, abort_flag, p.status))) break;
-        if (p.count > 1) {
-          const int pi = probs.find(u_lo + i);
-          if (pi != last_prob) { prefetch_tmap(&probs.get(pi).tmap_w); last_prob = pi; }
-        }
-        issue_w(i);
+        if (cw.prob != last_prob) { prefetch_tmap(&cw.pr->tmap_w); last_prob = cw.prob; }
+        issue_w();
         pw.next();
+        ++issued;
       }
-      if (!ok) {
-        // Abort path: let every weight copy already issued land before smem is released.
-        for (int s = 0; s < SW; ++s) {
-          mbar_wait_time(w_full(s), 0);
-          mbar_wait_time(w_full(s), 1);
-        }
-      }
+      if (!ok) drain_ring(w_full, SW, issued);
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------ X producer
@@ -303,47 +348,47 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       pdl_wait();                          // activations come from the previous kernel
       Pipe px{0, SX, 0};
       bool ok = true;
-      int last_prob = -1;
-      for (int i = 0; i < n_local; ++i) {
+      int last_prob = -1, issued = 0;
+      Cursor cx;
+      cx.init(probs, u_lo, u_hi);
+      for (int i = 0; i < n_local; ++i, cx.next()) {
         if (!(ok = wait_bar(x_empty(px.idx), px.phase ^ 1u, abort_flag, p.status))) break;
-        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
-        const TcProblem& pr = probs.get(ui.prob);
-        if (ui.prob != last_prob) { prefetch_tmap(&pr.tmap_x); last_prob = ui.prob; }
-        const int mt = ui.tile / pr.n_tiles;
+        const TcProblem& pr = *cx.pr;
+        if (cx.prob != last_prob) { prefetch_tmap(&pr.tmap_x); last_prob = cx.prob; }
         const uint32_t dst = s_x + px.idx * Cfg::X_STAGE;
         mbar_arrive_expect_tx(x_full(px.idx), Cfg::X_STAGE);
-        tma_load_2d(dst, &pr.tmap_x, ui.kb * kTcKBlock, mt * NMMA, x_full(px.idx));
-        tma_load_2d(dst + Cfg::X_ATOM, &pr.tmap_x, ui.kb * kTcKBlock + 64, mt * NMMA, x_full(px.idx));
+        tma_load_2d(dst, &pr.tmap_x, cx.kb * kTcKBlock, cx.mt * NMMA, x_full(px.idx));
+        tma_load_2d(dst + Cfg::X_ATOM, &pr.tmap_x, cx.kb * kTcKBlock + 64, cx.mt * NMMA, x_full(px.idx));
         px.next();
+        ++issued;
       }
-      if (!ok) {
-        for (int s = 0; s < SX; ++s) {
-          mbar_wait_time(x_full(s), 0);
-          mbar_wait_time(x_full(s), 1);
-        }
-      }
+      if (!ok) drain_ring(x_full, SX, issued);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp >= kTcWarps) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
+      constexpr int JPER = 8 / Cfg::NI;              // K steps of 16 per issuer and K block
+      const int w = warp == 1 ? 0 : warp - kTcWarps + 1;
       Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
       bool ok = true;
-      for (int i = 0; i < n_local && ok; ++i) {
-        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
-        const bool chunk_start = grouped<FMT>() ? true : ui.seg_start;
-        const bool chunk_end = grouped<FMT>() ? true : ui.seg_end;
+      Cursor cm;
+      cm.init(probs, u_lo, u_hi);
+      for (int i = 0; i < n_local && ok; ++i, cm.next()) {
+        const bool chunk_start = grouped<FMT>() ? true : cm.seg_start();
+        const bool chunk_end = grouped<FMT>() ? true : cm.seg_end();
         if (chunk_start && !(ok = wait_bar(d_empty(pd.idx), pd.phase ^ 1u, abort_flag, p.status))) break;
         if (!(ok = wait_bar(x_full(px.idx), px.phase, abort_flag, p.status))) break;
         if (!(ok = wait_bar(a_full(pa.idx), pa.phase, abort_flag, p.status))) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + Cfg::D_COL0 + pd.idx * Cfg::D_PITCH;
+        const uint32_t d_tmem = tmem + Cfg::d_col(pd.idx, w);
         const uint32_t a_tmem = tmem + 64u * pa.idx;
         const uint32_t xs = s_x + px.idx * Cfg::X_STAGE;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int jj = 0; jj < JPER; ++jj) {
+          const int j = w * JPER + jj;
           const uint64_t bdesc = smem_desc_sw128(xs + (j >> 2) * Cfg::X_ATOM + (j & 3) * 32);
-          tc_mma_ts(d_tmem, a_tmem + 8u * j, bdesc, idesc, (chunk_start && j == 0) ? 0u : 1u);
+          tc_mma_ts(d_tmem, a_tmem + 8u * j, bdesc, idesc, (chunk_start && jj == 0) ? 0u : 1u);
         }
         tc_commit(x_empty(px.idx));
         tc_commit(a_empty(pa.idx));
@@ -364,7 +409,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     const int h = (warp - 3) >> 2;          // which half of the K block (64 elements)
     const int r = q * 32 + lane;            // tile row owned by this thread
     Pipe pwc{0, SW, 0}, pa{0, A, 0};
-    for (int i = 0; i < n_local; ++i) {
+    Cursor cc_;
+    cc_.init(probs, u_lo, u_hi);
+    for (int i = 0; i < n_local; ++i, cc_.next()) {
       if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       const uint8_t* wrow = smem + L.w + pwc.idx * WSB + r * ROW_BYTES;
@@ -384,14 +431,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         }
       } else {
         // 64 nibbles = 2 chunks of 16 B; 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
-        const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
-        const TcProblem& pr = probs.get(ui.prob);
-        const int nt = ui.tile % pr.n_tiles;
-        int prow = E::phys_row(pr, nt, r);
+        const TcProblem& pr = *cc_.pr;
+        int prow = E::phys_row(pr, cc_.nt, r);
         prow = prow < pr.n ? prow : pr.n - 1;
         float z = 8.0f;
         if constexpr (FMT == KL_W4_ASYM)
-          z = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.zeros)[static_cast<long long>(prow) * ui.kb_total + ui.kb]);
+          z = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.zeros)[static_cast<long long>(prow) * cc_.kb_total + cc_.kb]);
         const uint32_t bias = XBF16 ? pack_bf16x2(-(128.0f + z), -(128.0f + z))
                                     : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
@@ -439,51 +484,67 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     float acc[grouped<FMT>() ? NMMA : 1];
     int seg_kb0 = 0;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const long long first_tile_u0 = n_local > 0 ? probs.info(u_lo, u_lo, u_hi).tile_u0 : 0;
+    // 16 columns of the accumulator: the sum of the NI issuers' partial D regions
+    auto load_d16 = [&](uint32_t d0, int cb, float (&v)[16]) {
+      uint32_t t[16];
+      tmem_ld16(d0 + 16u * cb, t);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(t[j]);
+#pragma unroll
+      for (int w = 1; w < Cfg::NI; ++w) {
+        tmem_ld16(d0 + static_cast<uint32_t>(w * Cfg::D_PITCH) + 16u * cb, t);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(t[j]);
+      }
+    };
+    Cursor ce;
+    ce.init(probs, u_lo, u_hi);
+    const long long first_tile_u0 = ce.tile_u0;
     bool ok = true;
-    for (int i = 0; i < n_local && ok; ++i) {
-      const UnitInfo ui = probs.info(u_lo + i, u_lo, u_hi);
-      const TcProblem& pr = probs.get(ui.prob);
-      const int mt = ui.tile / pr.n_tiles, nt = ui.tile % pr.n_tiles;
-      if (ui.seg_start) {
-        seg_kb0 = ui.kb;
+    for (int i = 0; i < n_local && ok; ++i, ce.next()) {
+      const TcProblem& pr = *ce.pr;
+      const int mt = ce.mt, nt = ce.nt;
+      const bool seg_end = ce.seg_end();
+      if (ce.seg_start()) {
+        seg_kb0 = ce.kb;
         if constexpr (grouped<FMT>()) {
 #pragma unroll
           for (int j = 0; j < NMMA; ++j) acc[j] = 0.f;
         }
       }
-      const bool chunk_end = grouped<FMT>() ? true : ui.seg_end;
+      const bool chunk_end = grouped<FMT>() ? true : seg_end;
       if (!chunk_end) continue;
       if (!(ok = wait_bar(d_full(pd.idx), pd.phase, abort_flag, p.status))) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + lane_base + Cfg::D_COL0 + pd.idx * Cfg::D_PITCH;
+      const uint32_t d_tmem = tmem + lane_base + Cfg::d_col(pd.idx, 0);
       const int prow = E::phys_row(pr, nt, r);
-      const bool full_tile = ui.seg_end && seg_kb0 == 0 && ui.kb == ui.kb_total - 1;
+      const bool full_tile = seg_end && seg_kb0 == 0 && ce.kb == ce.kb_total - 1;
       float* part_base = nullptr;
-      if (ui.seg_end && !full_tile) {
-        const int slot = (ui.tile_u0 == first_tile_u0) ? 0 : 1;
+      if (seg_end && !full_tile) {
+        const int slot = (ce.tile_u0 == first_tile_u0) ? 0 : 1;
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
       }
       if constexpr (grouped<FMT>()) {
         const int pr_row = prow < pr.n ? prow : pr.n - 1;
         float s;
         if constexpr (FMT == KL_W4_ASYM)
-          s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ui.kb_total + ui.kb]);
+          s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb]);
         else
-          s = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ui.kb_total + ui.kb];
+          s = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb];
 #pragma unroll
         for (int cb = 0; cb < NMMA / 16; ++cb) {
-          uint32_t v[16];
-          tmem_ld16(d_tmem + 16u * cb, v);
-          tc_wait_ld();
+          float v[16];
+          load_d16(d_tmem, cb, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, __uint_as_float(v[j]), acc[cb * 16 + j]);
+          for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, v[j], acc[cb * 16 + j]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_empty(pd.idx));
         pd.next();
-        if (!ui.seg_end) continue;
+        if (!seg_end) continue;
         if (full_tile) {
 #pragma unroll
           for (int cb = 0; cb < NMMA / 16; ++cb) {
@@ -501,17 +562,16 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       } else {
         const float s = E::row_scale(pr, prow);
         for (int cb = 0; cb < NMMA / 16; ++cb) {
-          uint32_t v[16];
-          tmem_ld16(d_tmem + 16u * cb, v);
-          tc_wait_ld();
+          float v[16];
+          load_d16(d_tmem, cb, v);
           if (full_tile) {
             float o[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = __uint_as_float(v[j]) * s;
+            for (int j = 0; j < 16; ++j) o[j] = v[j] * s;
             E::emit16(pr, mt, nt, r, cb, o, xch);
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = __uint_as_float(v[j]);
+            for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[j];
           }
         }
         tc_fence_before();
@@ -521,8 +581,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         if (full_tile) continue;
       }
       // ---- split tile: publish the partial, the last contributor finishes it.
-      const long long c_first = unit_owner(ui.tile_u0, p.units, G);
-      const long long c_last = unit_owner(ui.tile_u0 + ui.kb_total - 1, p.units, G);
+      const long long c_first = unit_owner(ce.tile_u0, p.units, G);
+      const long long c_last = unit_owner(ce.tile_u0 + ce.kb_total - 1, p.units, G);
       __threadfence();
       named_bar_epi();
       if (threadIdx.x == kFirstEpiThread) {
@@ -544,7 +604,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
 #pragma unroll 4
         for (long long cc = c_first; cc <= c_last; ++cc) {
           // slot 0 holds a contributor's first tile: the one its range starts in
-          const int sl = unit_lo(cc, p.units, G) >= ui.tile_u0 ? 0 : 1;
+          const int sl = unit_lo(cc, p.units, G) >= ce.tile_u0 ? 0 : 1;
           const float* src = p.partials + (cc * 2 + sl) * static_cast<long long>(NMMA) * 128 + cb * 16 * 128 + r;
           float t[16];
 #pragma unroll
@@ -582,7 +642,7 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(plan.grid);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(TcCfg<NMMA>::THREADS);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -617,6 +677,15 @@ cudaError_t launch_fmt(const TcParams& p, const TcPlan& plan, int fmt, bool pdl,
 
 }  // namespace
 
+int tc_threads(int n_mma) {
+  switch (n_mma) {
+    case 16: return TcCfg<16>::THREADS;
+    case 32: return TcCfg<32>::THREADS;
+    case 64: return TcCfg<64>::THREADS;
+    default: return TcCfg<128>::THREADS;
+  }
+}
+
 int tc_choose_nmma(int m, int fmt) {
   const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
   const int n = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
@@ -640,7 +709,7 @@ TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count) {
   t.grid = static_cast<int>(std::min<long long>(units, sm_count));
   const int wsb = w4 ? 8192 : 16384;
   const int x_stage = 2 * n_mma * 128;
-  const int a_stages = n_mma == 128 ? 4 : 6;
+  const int a_stages = 4;
   t.x_stages = n_mma == 128 ? 3 : 4;
   const int budget = 220 * 1024;
   int sw = kMaxWStages;
