@@ -109,7 +109,7 @@ bool tc_shape_ok(int k, int w_format, int group) {
 // Fill one tcgen05 problem (tensor maps + fields); the caller sets unit_begin.
 int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n,
                   const void* scales, const void* zeros, int swiglu, void* y, bool transposed, long long ldy,
-                  int n_mma) {
+                  int n_mma, int kblk) {
   std::memset(&pr, 0, sizeof(pr));
   int rc;
   if (is_w4(w_format))
@@ -129,19 +129,24 @@ int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
   pr.y_transposed = transposed ? 1 : 0;
-  tc_problem_tiles(pr, n_mma, swiglu != 0);
+  tc_problem_tiles(pr, n_mma, kblk, swiglu != 0);
   return KL_OK;
 }
 
 // Units of one problem without building its tensor maps (host planning only).
-long long problem_units(int m, int n, int k, int n_mma, bool swiglu) {
+long long problem_units(int m, int n, int k, int n_mma, int kblk, bool swiglu) {
   TcProblem pr;
   std::memset(&pr, 0, sizeof(pr));
   pr.m = m;
   pr.n = n;
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
-  return tc_problem_tiles(pr, n_mma, swiglu);
+  return tc_problem_tiles(pr, n_mma, kblk, swiglu);
+}
+
+// K block for one GEMM on this device.
+int choose_kblk_single(int m, int n, int k, int fmt, int n_mma, bool swiglu, int sm_count) {
+  return tc_choose_kblk(fmt, n_mma, problem_units(m, n, k, n_mma, 256, swiglu), sm_count);
 }
 
 int validate_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
@@ -197,7 +202,8 @@ size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, 
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;
   const int n_mma = tc_choose_nmma(mm, w_format);
-  const TcPlan plan = plan_tc(n_mma, problem_units(mm, n, k, n_mma, swiglu != 0), w_format, sm);
+  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm);
+  const TcPlan plan = plan_tc(n_mma, kblk, problem_units(mm, n, k, n_mma, kblk, swiglu != 0), w_format, sm);
   return plan.ok ? plan.workspace : 0;
 }
 
@@ -226,16 +232,17 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     for (int m0 = 0; m0 < m; m0 += mchunk) {
       const int mm = std::min(mchunk, m - m0);
       const int n_mma = tc_choose_nmma(mm, w_format);
+      const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, di.sm_count);
       TcParams p;
       std::memset(&p, 0, sizeof(p));
       const char* xb = static_cast<const char*>(x) + static_cast<size_t>(m0) * k * eb;
       char* yb = static_cast<char*>(y) + (transposed ? static_cast<size_t>(m0) : static_cast<size_t>(m0) * n_out) * eb;
       rc = build_problem(p.single, xb, x_dtype, mm, k, w, w_format, n, scales, zeros, swiglu, yb, transposed,
-                         transposed ? m : n_out, n_mma);
+                         transposed ? m : n_out, n_mma, kblk);
       if (rc != KL_OK) return rc;
       p.single.unit_begin = 0;
       const long long units = static_cast<long long>(p.single.m_tiles) * p.single.n_tiles * p.single.kb_total;
-      const TcPlan plan = plan_tc(n_mma, units, w_format, di.sm_count);
+      const TcPlan plan = plan_tc(n_mma, kblk, units, w_format, di.sm_count);
       if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for m=%d n=%d k=%d", mm, n, k);
       if (!workspace || workspace_bytes < plan.workspace)
         return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
@@ -279,7 +286,8 @@ struct GroupHeader {
   uint32_t magic, count;
   int n_mma, w_format, swiglu, x_dtype;
   long long units;
-  uint8_t pad[256 - 32];
+  int kblk;
+  uint8_t pad[256 - 36];
 };
 static_assert(sizeof(GroupHeader) == 256, "group header");
 constexpr uint32_t kGroupMagic = 0x4B4C4752u;   // "KLGR"
@@ -318,12 +326,21 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
   hd->swiglu = swiglu ? 1 : 0;
   hd->x_dtype = x_dtype;
   TcProblem* tab = reinterpret_cast<TcProblem*>(hd + 1);
+  int sm = 148, dev = 0, v = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+    sm = v;
+  else
+    cudaGetLastError();
+  long long units256 = 0;
+  for (int i = 0; i < count; ++i)
+    units256 += problem_units(problems[i].m, problems[i].n, problems[i].k, hd->n_mma, 256, swiglu != 0);
+  hd->kblk = tc_choose_kblk(w_format, hd->n_mma, units256, sm);
   long long units = 0;
   for (int i = 0; i < count; ++i) {
     const kl_problem& q = problems[i];
     const int n_out = swiglu ? q.n / 2 : q.n;
     int rc = build_problem(tab[i], q.x, x_dtype, q.m, q.k, q.w, w_format, q.n, q.scales, q.zeros, swiglu, q.y, false,
-                           n_out, hd->n_mma);
+                           n_out, hd->n_mma, hd->kblk);
     if (rc != KL_OK) return rc;
     tab[i].unit_begin = units;
     units += static_cast<long long>(tab[i].m_tiles) * tab[i].n_tiles * tab[i].kb_total;
@@ -340,7 +357,7 @@ size_t kl_grouped_workspace_bytes(const void* host_table) {
     sm = v;
   else
     cudaGetLastError();
-  const TcPlan plan = plan_tc(hd->n_mma, hd->units, hd->w_format, sm);
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->w_format, sm);
   return plan.ok ? plan.workspace : 0;
 }
 
@@ -355,7 +372,7 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
   if (rc != KL_OK) return rc;
   if (!(di.major == 10 && di.minor == 0))
     return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
-  const TcPlan plan = plan_tc(hd->n_mma, hd->units, hd->w_format, di.sm_count);
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->w_format, di.sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for the group");
   if (!workspace || workspace_bytes < plan.workspace)
     return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
@@ -507,12 +524,13 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
   pr.n = n;
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
-  const long long units = tc_problem_tiles(pr, n_mma, swiglu != 0);
-  const TcPlan plan = plan_tc(n_mma, units, w_format, sm_count);
+  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm_count);
+  const long long units = tc_problem_tiles(pr, n_mma, kblk, swiglu != 0);
+  const TcPlan plan = plan_tc(n_mma, kblk, units, w_format, sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan");
   out[0] = 2;
   out[1] = plan.grid;
-  out[2] = tc_threads(plan.n_mma);
+  out[2] = tc_threads(plan.n_mma, plan.kblk);
   out[3] = plan.smem;
   out[4] = plan.n_mma;
   out[5] = plan.w_stages;

@@ -32,7 +32,6 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& p, int fmt, bool swig
 // tile) converted to bf16/f16 into tensor memory as the MMA's A operand and X
 // (n_mma tokens per tile) TMA-staged in shared memory as the B operand.
 constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
-constexpr int kTcKBlock = 128;        // K elements per pipeline stage
 constexpr int kTcWarps = 15;          // W-TMA, MMA, X-TMA, 8 converter, 4 epilogue warps (+ extra MMA issuers)
 constexpr int kCounterBytes = 64 * 1024;
 constexpr int kMaxDevices = 64;
@@ -66,15 +65,19 @@ struct TcParams {
 
 struct TcPlan {
   bool ok;
-  int n_mma, w_stages, x_stages, grid, smem;
+  int n_mma, kblk, w_stages, x_stages, grid, smem;
   long long units;
   size_t workspace;                   // counters + partials
 };
 int tc_choose_nmma(int m, int fmt);
-int tc_threads(int n_mma);           // block size of the tcgen05 kernel for this token tile
-// Fill the tiling fields of a problem (m_tiles, n_tiles, kb_total); returns its unit count.
-long long tc_problem_tiles(TcProblem& pr, int n_mma, bool swiglu);
-TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count);
+int tc_threads(int n_mma, int kblk);  // block size of the tcgen05 kernel for this token tile
+// Fill the tiling fields of a problem (m_tiles, n_tiles, kb_total) for K blocks
+// of kblk elements; returns its unit count.
+long long tc_problem_tiles(TcProblem& pr, int n_mma, int kblk, bool swiglu);
+// K elements per pipeline stage: 256 for the int8 decode path when the work
+// keeps every SM busy (fewer hand-offs per byte), else 128.
+int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count);
+TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count);
 cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
 // Work partition shared by the kernel and the host-side self-check:

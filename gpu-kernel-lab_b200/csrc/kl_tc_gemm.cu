@@ -49,23 +49,30 @@ namespace {
 // bounds the weight stream.  Each K block's 8 MMAs are therefore split across
 // NI issuing threads (separate warps), each accumulating into its own TMEM
 // region; the epilogue adds the NI partial accumulators.
-template <int NMMA>
+template <int NMMA, int KBL>
 struct TcCfg {
-  static constexpr int NI = NMMA <= 32 ? 4 : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
+  static constexpr int NI = NMMA <= 32 ? (KBL == 256 ? 2 : 4) : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
   static constexpr int THREADS = (kTcWarps + NI - 1) * 32;
-  static constexpr int A_STAGES = 4;
+  static constexpr int ACOLS = KBL / 2;                      // TMEM columns of one A stage (bf16 pairs)
   static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D accumulator
-  static constexpr int D_COL0 = 64 * A_STAGES;               // A stages first (64 cols each)
+  static constexpr int A_STAGES_FIT = (512 - 2 * NI * D_PITCH) / ACOLS;
+  static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
+  static constexpr int D_COL0 = ACOLS * A_STAGES;            // A stages first
   static constexpr int TMEM_COLS = 512;
-  static_assert(D_COL0 + 2 * NI * D_PITCH <= TMEM_COLS, "TMEM budget");
+  static_assert(A_STAGES >= 2 && D_COL0 + 2 * NI * D_PITCH <= TMEM_COLS, "TMEM budget");
   // D accumulator of buffer b (0/1) and issuer w
   static constexpr uint32_t d_col(int b, int w) { return D_COL0 + (b * NI + w) * D_PITCH; }
+  static constexpr int KSTEPS = KBL / 16;                    // MMAs (K = 16 each) per stage
   static constexpr int X_ATOM = NMMA * 128;                  // bytes: NMMA rows x 64 bf16
-  static constexpr int X_STAGE = 2 * X_ATOM;
+  static constexpr int X_ATOMS = KBL / 64;
+  static constexpr int X_STAGE = X_ATOMS * X_ATOM;
 };
 
 template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL_W4_ASYM; }
-template <int FMT> constexpr int w_stage_bytes() { return is_w4<FMT>() ? 8192 : 16384; }
+// Weight stage: 128 rows x KBL elements, stored as column blocks of one
+// swizzle span (128 B of int8 / 64 B of packed int4) by 128 rows.
+template <int FMT, int KBL> constexpr int w_row_bytes() { return is_w4<FMT>() ? KBL / 2 : KBL; }
+template <int FMT, int KBL> constexpr int w_stage_bytes() { return 128 * w_row_bytes<FMT, KBL>(); }
 template <int FMT> constexpr bool grouped() { return is_w4<FMT>(); }
 
 constexpr int kXchBytes = 64 * 16 * 4;            // SwiGLU up-value exchange: 64 rows x 16 cols f32
@@ -249,13 +256,17 @@ struct Epi {
   }
 };
 
-template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
-__global__ void __launch_bounds__(TcCfg<NMMA>::THREADS, 1)
+template <int FMT, int NMMA, int KBL, bool SWIGLU, bool XBF16>
+__global__ void __launch_bounds__(TcCfg<NMMA, KBL>::THREADS, 1)
 tc_qgemm_kernel(const __grid_constant__ TcParams p) {
-  using Cfg = TcCfg<NMMA>;
+  using Cfg = TcCfg<NMMA, KBL>;
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
-  constexpr int WSB = w_stage_bytes<FMT>();
-  constexpr int ROW_BYTES = is_w4<FMT>() ? 64 : 128;     // bytes of one tile row per stage
+  static_assert(!grouped<FMT>() || KBL == 128, "4-bit group mode: one group of 128 per stage");
+  constexpr int WSB = w_stage_bytes<FMT, KBL>();
+  constexpr int ROW_BYTES = w_row_bytes<FMT, KBL>();      // bytes of one tile row per stage
+  constexpr int SPAN = is_w4<FMT>() ? 64 : 128;           // swizzle span = TMA box inner bytes
+  constexpr int NBLK = ROW_BYTES / SPAN;                  // column blocks per stage
+  constexpr int BLK = 128 * SPAN;                         // bytes of one column block
   constexpr int A = Cfg::A_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -300,8 +311,11 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     mbar_arrive_expect_tx(w_full(pw.idx), WSB);
     const int y0 = SWIGLU ? cw.nt * 64 : cw.nt * 128;
     const int y1 = SWIGLU ? pr.n_out + cw.nt * 64 : cw.nt * 128 + 64;
-    tma_load_2d(dst, &pr.tmap_w, cw.kb * ROW_BYTES, y0, w_full(pw.idx));
-    tma_load_2d(dst + WSB / 2, &pr.tmap_w, cw.kb * ROW_BYTES, y1, w_full(pw.idx));
+#pragma unroll
+    for (int b = 0; b < NBLK; ++b) {
+      tma_load_2d(dst + b * BLK, &pr.tmap_w, cw.kb * ROW_BYTES + b * SPAN, y0, w_full(pw.idx));
+      tma_load_2d(dst + b * BLK + BLK / 2, &pr.tmap_w, cw.kb * ROW_BYTES + b * SPAN, y1, w_full(pw.idx));
+    }
     cw.next();
   };
   if (threadIdx.x == 0) {
@@ -357,8 +371,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         if (cx.prob != last_prob) { prefetch_tmap(&pr.tmap_x); last_prob = cx.prob; }
         const uint32_t dst = s_x + px.idx * Cfg::X_STAGE;
         mbar_arrive_expect_tx(x_full(px.idx), Cfg::X_STAGE);
-        tma_load_2d(dst, &pr.tmap_x, cx.kb * kTcKBlock, cx.mt * NMMA, x_full(px.idx));
-        tma_load_2d(dst + Cfg::X_ATOM, &pr.tmap_x, cx.kb * kTcKBlock + 64, cx.mt * NMMA, x_full(px.idx));
+#pragma unroll
+        for (int a = 0; a < Cfg::X_ATOMS; ++a)
+          tma_load_2d(dst + a * Cfg::X_ATOM, &pr.tmap_x, cx.kb * KBL + 64 * a, cx.mt * NMMA, x_full(px.idx));
         px.next();
         ++issued;
       }
@@ -368,7 +383,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
-      constexpr int JPER = 8 / Cfg::NI;              // K steps of 16 per issuer and K block
+      constexpr int JPER = Cfg::KSTEPS / Cfg::NI;    // K steps of 16 per issuer and stage
       const int w = warp == 1 ? 0 : warp - kTcWarps + 1;
       Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
       bool ok = true;
@@ -382,7 +397,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         if (!(ok = wait_bar(a_full(pa.idx), pa.phase, abort_flag, p.status))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + Cfg::d_col(pd.idx, w);
-        const uint32_t a_tmem = tmem + 64u * pa.idx;
+        const uint32_t a_tmem = tmem + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx;
         const uint32_t xs = s_x + px.idx * Cfg::X_STAGE;
 #pragma unroll
         for (int jj = 0; jj < JPER; ++jj) {
@@ -414,14 +429,16 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     for (int i = 0; i < n_local; ++i, cc_.next()) {
       if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
-      const uint8_t* wrow = smem + L.w + pwc.idx * WSB + r * ROW_BYTES;
-      uint32_t out[32];
+      constexpr int EPT = KBL / 2;                 // elements per thread (half a stage row)
+      const uint8_t* wstage = smem + L.w + pwc.idx * WSB;
+      uint32_t out[EPT / 2];
       if constexpr (!is_w4<FMT>()) {
-        // 64 int8 = 4 chunks of 16 B; 128B swizzle: chunk c at c ^ (r & 7)
+        // EPT int8 = EPT/16 chunks of 16 B; chunk g of the stage row sits in column
+        // block g/8 at position (g%8) ^ (r & 7) (128B swizzle)
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int chunk = 4 * h + cc;
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((chunk ^ (r & 7)) << 4));
+        for (int cc = 0; cc < EPT / 16; ++cc) {
+          const int g = h * (EPT / 16) + cc;
+          const uint4 v = *reinterpret_cast<const uint4*>(wstage + (g >> 3) * BLK + r * 128 + (((g & 7) ^ (r & 7)) << 4));
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
@@ -430,7 +447,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
           }
         }
       } else {
-        // 64 nibbles = 2 chunks of 16 B; 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
+        // EPT nibbles = EPT/32 chunks of 16 B; 64B swizzle: chunk g at g ^ ((r >> 1) & 3)
         const TcProblem& pr = *cc_.pr;
         int prow = E::phys_row(pr, cc_.nt, r);
         prow = prow < pr.n ? prow : pr.n - 1;
@@ -442,9 +459,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
                                          : (FMT == KL_W4_SYM ? 0x64086408u : 0x64006400u);
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int chunk = 2 * h + cc;
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((chunk ^ ((r >> 1) & 3)) << 4));
+        for (int cc = 0; cc < EPT / 32; ++cc) {
+          const int g = h * (EPT / 32) + cc;
+          const uint4 v = *reinterpret_cast<const uint4*>(wstage + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
@@ -457,9 +474,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
           }
         }
       }
-      const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + 64u * pa.idx + 32u * h;
+      const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
+                              static_cast<uint32_t>(EPT / 2) * h;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < EPT / 32; ++j) {
         uint32_t part[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) part[t] = out[16 * j + t];
@@ -625,9 +643,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
-template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
+template <int FMT, int NMMA, int KBL, bool SWIGLU, bool XBF16>
 cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStream_t s) {
-  auto kern = tc_qgemm_kernel<FMT, NMMA, SWIGLU, XBF16>;
+  auto kern = tc_qgemm_kernel<FMT, NMMA, KBL, SWIGLU, XBF16>;
   static std::atomic<int> smem_set[kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -642,7 +660,7 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(plan.grid);
-  cfg.blockDim = dim3(TcCfg<NMMA>::THREADS);
+  cfg.blockDim = dim3(TcCfg<NMMA, KBL>::THREADS);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -655,13 +673,24 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
 
 template <int FMT, bool SWIGLU, bool XBF16>
 cudaError_t launch_nmma(const TcParams& p, const TcPlan& plan, bool pdl, cudaStream_t s) {
+  if constexpr (FMT == KL_W8_ROW) {
+    if (plan.kblk == 256) {
+      switch (plan.n_mma) {
+        case 16: return launch_one<FMT, 16, 256, SWIGLU, XBF16>(p, plan, pdl, s);
+        case 32: return launch_one<FMT, 32, 256, SWIGLU, XBF16>(p, plan, pdl, s);
+        case 64: return launch_one<FMT, 64, 256, SWIGLU, XBF16>(p, plan, pdl, s);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+  }
+  if (plan.kblk != 128) return cudaErrorInvalidValue;
   switch (plan.n_mma) {
-    case 16: return launch_one<FMT, 16, SWIGLU, XBF16>(p, plan, pdl, s);
-    case 32: return launch_one<FMT, 32, SWIGLU, XBF16>(p, plan, pdl, s);
-    case 64: return launch_one<FMT, 64, SWIGLU, XBF16>(p, plan, pdl, s);
+    case 16: return launch_one<FMT, 16, 128, SWIGLU, XBF16>(p, plan, pdl, s);
+    case 32: return launch_one<FMT, 32, 128, SWIGLU, XBF16>(p, plan, pdl, s);
+    case 64: return launch_one<FMT, 64, 128, SWIGLU, XBF16>(p, plan, pdl, s);
     default:
       if constexpr (grouped<FMT>()) return cudaErrorInvalidValue;   // group mode keeps <= 64 columns in registers
-      else return launch_one<FMT, 128, SWIGLU, XBF16>(p, plan, pdl, s);
+      else return launch_one<FMT, 128, 128, SWIGLU, XBF16>(p, plan, pdl, s);
   }
 }
 
@@ -677,13 +706,30 @@ cudaError_t launch_fmt(const TcParams& p, const TcPlan& plan, int fmt, bool pdl,
 
 }  // namespace
 
-int tc_threads(int n_mma) {
-  switch (n_mma) {
-    case 16: return TcCfg<16>::THREADS;
-    case 32: return TcCfg<32>::THREADS;
-    case 64: return TcCfg<64>::THREADS;
-    default: return TcCfg<128>::THREADS;
+int tc_threads(int n_mma, int kblk) {
+  if (kblk == 256) {
+    switch (n_mma) {
+      case 16: return TcCfg<16, 256>::THREADS;
+      case 32: return TcCfg<32, 256>::THREADS;
+      default: return TcCfg<64, 256>::THREADS;
+    }
   }
+  switch (n_mma) {
+    case 16: return TcCfg<16, 128>::THREADS;
+    case 32: return TcCfg<32, 128>::THREADS;
+    case 64: return TcCfg<64, 128>::THREADS;
+    default: return TcCfg<128, 128>::THREADS;
+  }
+}
+
+static int tc_a_stages(int n_mma, int kblk) {
+  if (kblk == 256) return n_mma <= 32 ? TcCfg<16, 256>::A_STAGES : TcCfg<64, 256>::A_STAGES;
+  return 4;
+}
+
+int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count) {
+  if (fmt != KL_W8_ROW || n_mma > 64) return 128;
+  return units_at_256 >= 2ll * sm_count ? 256 : 128;
 }
 
 int tc_choose_nmma(int m, int fmt) {
@@ -692,27 +738,30 @@ int tc_choose_nmma(int m, int fmt) {
   return (w4 && n > 64) ? 64 : n;     // group mode: the host splits M into 64-token launches
 }
 
-long long tc_problem_tiles(TcProblem& pr, int n_mma, bool swiglu) {
+long long tc_problem_tiles(TcProblem& pr, int n_mma, int kblk, bool swiglu) {
   pr.m_tiles = (pr.m + n_mma - 1) / n_mma;
   pr.n_tiles = swiglu ? (pr.n_out + 63) / 64 : (pr.n + 127) / 128;
-  pr.kb_total = (pr.k + kTcKBlock - 1) / kTcKBlock;
+  pr.kb_total = (pr.k + kblk - 1) / kblk;
   return static_cast<long long>(pr.m_tiles) * pr.n_tiles * pr.kb_total;
 }
 
-TcPlan plan_tc(int n_mma, long long units, int fmt, int sm_count) {
+TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   TcPlan t{};
   t.ok = false;
   if (units <= 0 || sm_count <= 0) return t;
   const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
+  if (!(kblk == 128 || (kblk == 256 && fmt == KL_W8_ROW && n_mma <= 64))) return t;
   t.n_mma = n_mma;
+  t.kblk = kblk;
   t.units = units;
   t.grid = static_cast<int>(std::min<long long>(units, sm_count));
-  const int wsb = w4 ? 8192 : 16384;
-  const int x_stage = 2 * n_mma * 128;
-  const int a_stages = 4;
-  t.x_stages = n_mma == 128 ? 3 : 4;
+  const int wsb = 128 * (w4 ? kblk / 2 : kblk);
+  const int x_stage = (kblk / 64) * n_mma * 128;
+  const int a_stages = tc_a_stages(n_mma, kblk);
+  t.x_stages = n_mma == 128 ? 3 : (x_stage > 16384 ? 3 : 4);
+  // ~128 KB of weights in flight per SM: deeper rings over-subscribe HBM
   const int budget = 220 * 1024;
-  int sw = kMaxWStages;
+  int sw = std::max(2, std::min(kMaxWStages, (128 * 1024) / wsb));
   while (sw > 2 && static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total) > budget) --sw;
   t.w_stages = sw;
   t.smem = static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total);

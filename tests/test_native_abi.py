@@ -62,7 +62,7 @@ def test_plan_partition_w8(kl, m, n, k):
     assert plan["smem"] <= 227 * 1024
     assert plan["n_mma"] in (16, 32, 64, 128)
     if m <= 64:
-        assert plan["stages"] >= 8          # deep weight ring: >= 128 KB of weights in flight per SM
+        assert plan["stages"] >= 3          # weight ring of >= 3 stages (16-32 KB each) per SM
 
 
 @pytest.mark.parametrize("m", [1, 16, 64])
