@@ -208,6 +208,10 @@ def build_weights(kl, shapes, layers, device, seed=1234):
 
 
 def bench_decode(args, kl, world, rank, local, dist):
+    """Config 1 (or 4 with --workload llama): every projection of the decode step
+    at each batch size M.  The step runs each M as ONE grouped tcgen05 launch
+    over all 113 (independent) GEMMs; the same GEMMs launched one by one in
+    model order (PDL-chained CUDA graph) are reported as ``chain``."""
     import torch
     device = torch.device("cuda", local)
     layer, head = (LLAMA_LAYER, LLAMA_HEAD) if args.workload == "llama" else (QWEN_LAYER, QWEN_HEAD)
@@ -219,7 +223,6 @@ def bench_decode(args, kl, world, rank, local, dist):
     weights.append(("lm_head", kl.quantize_int8_rowwise(hw)))
     del hw
     torch.cuda.empty_cache()
-    shard = None
 
     xg = torch.Generator(device=device)
     xg.manual_seed(99 + rank)
@@ -233,28 +236,33 @@ def bench_decode(args, kl, world, rank, local, dist):
             items.append((name, p, x, y))
         passes[m] = items
 
-    def run_pass(m):
+    def pass_bytes(m):
+        return sum(p.data.shape[0] * p.data.shape[1] + 2 * p.data.shape[0] + 2 * m * p.data.shape[1]
+                   + 2 * m * p.data.shape[0] for _, p, _, _ in passes[m])
+
+    grouped = {m: kl.GroupedLinear([(x, p, y) for _, p, x, y in passes[m]]) for m in ms_list}
+
+    def run_grouped(m):
+        grouped[m].run(pdl=True)
+
+    def run_chain(m):
         for name, p, x, y in passes[m]:
             kl.quant_linear(x, p, out=y, pdl=True)
 
-    # algorithmic bytes of one pass at each M
-    def pass_bytes(m):
-        b = 0
-        for name, p, x, y in passes[m]:
-            n, k = p.data.shape
-            b += n * k + 2 * n + 2 * m * k + 2 * m * n
-        return b
-
-    launches_per_pass = {m: len(passes[m]) for m in ms_list}
     for m in ms_list:                 # eager warm-up (allocates the workspace before capture)
-        run_pass(m)
+        run_grouped(m)
+        run_chain(m)
     torch.cuda.synchronize()
-    graphs = {}
-    for m in ms_list:
+
+    def capture(fn):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            run_pass(m)
-        graphs[m] = g
+            fn()
+        return g
+
+    step_graph = capture(lambda: [run_grouped(m) for m in ms_list])
+    per_m_graph = {m: capture(lambda m=m: run_grouped(m)) for m in ms_list}
+    chain_graph = {m: capture(lambda m=m: run_chain(m)) for m in ms_list}
     torch.cuda.synchronize()
 
     def barrier():
@@ -262,11 +270,18 @@ def bench_decode(args, kl, world, rank, local, dist):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def timed(graph, reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
     for _ in range(args.warmup):
-        for m in ms_list:
-            graphs[m].replay()
+        step_graph.replay()
     barrier()
-    ev = {m: [] for m in ms_list}
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -274,24 +289,26 @@ def bench_decode(args, kl, world, rank, local, dist):
         barrier()
         start.record()
         for _ in range(args.steps):
-            for m in ms_list:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-                graphs[m].replay()
-                e1.record()
-                ev[m].append((e0, e1))
+            step_graph.replay()
         stop.record()
         barrier()
-    total_ms = start.elapsed_time(stop)
-    per_m_ms = {m: sum(a.elapsed_time(b) for a, b in ev[m]) / args.steps for m in ms_list}
-    ms_step = total_ms / args.steps
+    ms_step = start.elapsed_time(stop) / args.steps
     if dist is not None:
         t = torch.tensor([ms_step], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = t.item()
     step_bytes = sum(pass_bytes(m) for m in ms_list)
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
+
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    per_m = {}
+    for m in ms_list:
+        t_g = timed(per_m_graph[m], max(3, args.steps // 2))
+        t_c = timed(chain_graph[m], max(3, args.steps // 2))
+        b = pass_bytes(m)
+        per_m[str(m)] = {"grouped_ms": round(t_g, 4), "grouped_GB/s": round(b / (t_g * 1e-3) / 1e9, 1),
+                         "frac_hbm": round(b / (t_g * 1e-3) / 1e9 / hbm, 3),
+                         "chain_ms": round(t_c, 4), "chain_GB/s": round(b / (t_c * 1e-3) / 1e9, 1)}
 
     # ---- e2e through the public API with host buffers
     pinned = {m: [torch.empty(x.shape, dtype=x.dtype, pin_memory=True).copy_(x) for _, _, x, _ in passes[m]]
@@ -304,7 +321,7 @@ def bench_decode(args, kl, world, rank, local, dist):
         for m in ms_list:
             for (name, p, x, y), hx in zip(passes[m], pinned[m]):
                 x.copy_(hx, non_blocking=True)
-            graphs[m].replay()
+            per_m_graph[m].replay()
             head_out[m].copy_(passes[m][-1][3], non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -323,49 +340,36 @@ def bench_decode(args, kl, world, rank, local, dist):
         e2e_ms = t.item()
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
 
-    # ---- dominant kernel alone: the lm_head launch (largest single GEMM), L2-cold
-    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
+    # ---- the largest single GEMM alone (lm_head, M = first batch size), graph-timed
     name, p, x, y = passes[ms_list[0]][-1]
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    times = []
-    for i in range(8):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        kl.quant_linear(x, p, out=y)
-        b.record()
-        torch.cuda.synchronize()
-        if i >= 2:
-            times.append(a.elapsed_time(b))
+    head_graph = capture(lambda: [kl.quant_linear(x, p, out=y, pdl=True) for _ in range(5)])
+    head_ms = timed(head_graph, 4) / 5
     n, k = p.data.shape
     m0 = ms_list[0]
-    head_bytes = n * k + 2 * n + 2 * m0 * k + 2 * m0 * n
-    head_ms = statistics.median(times)
-    head_gbs = head_bytes / (head_ms * 1e-3) / 1e9
+    head_gbs = (n * k + 2 * n + 2 * m0 * k + 2 * m0 * n) / (head_ms * 1e-3) / 1e9
 
+    achieved = step_bytes / (ms_step * 1e-3) / 1e9
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": ("llama-3.2-3b" if args.workload == "llama" else "qwen3-0.6b") +
                                " decode projection set (BASELINE config " + ("4" if args.workload == "llama" else "1") + ")",
-                   "batch_m": ms_list, "gemms_per_pass": launches_per_pass[ms_list[0]],
+                   "batch_m": ms_list, "gemms_per_pass": len(passes[ms_list[0]]),
                    "bytes_per_step": step_bytes, "weights": "int8 per-row bf16 scale, N(0,0.02) seeded",
                    "l2": "inputs larger than L2: each pass streams >=0.6 GB of weights, no flush needed",
-                   "parallelism": f"replicas x{world}" + (" + vocab-sharded lm_head (NCCL all-gather)" if shard else ""),
-                   "launch": "CUDA graph per M, kernels chained with programmatic dependent launch"},
-        "per_m": {str(m): {"ms": round(per_m_ms[m], 4), "GB/s": round(pass_bytes(m) / (per_m_ms[m] * 1e-3) / 1e9, 1),
-                           "frac_hbm": round(pass_bytes(m) / (per_m_ms[m] * 1e-3) / 1e9 / hbm, 3)}
-                  for m in ms_list},
-        "roofline": {"bound": "hbm", "kernel": "tc_qgemm_kernel (every launch of the step)",
-                     "achieved": round(step_bytes / (ms_step * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4), "peak_source": peak_kind,
+                   "parallelism": f"replicas x{world}",
+                   "launch": "one grouped tcgen05 launch per M (113 independent GEMMs), CUDA graph"},
+        "per_m": per_m,
+        "roofline": {"bound": "hbm", "kernel": "tc_qgemm_kernel (the step's 4 grouped launches)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
                      "traffic": profiled_traffic(f"{args.workload}_step"),
                      "lm_head_alone": {"ms": round(head_ms, 4), "GB/s": round(head_gbs, 1),
                                        "frac": round(head_gbs / hbm, 3), "m": m0}},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": sum(launches_per_pass.values()) * args.steps,
+        "gpu_launches": len(ms_list) * args.steps,
         "clocks": clocks.summary(),
     }
     return result

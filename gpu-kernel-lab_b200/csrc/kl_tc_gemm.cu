@@ -577,6 +577,35 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         for (int cb = 0; cb < NMMA / 16; ++cb)
 #pragma unroll
           for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
+      } else if constexpr (NMMA <= 64) {
+        // Pull the whole accumulator into registers and hand the TMEM buffer
+        // back to the MMA issuers before the (slower) global stores.
+        const float s = E::row_scale(pr, prow);
+        float v[NMMA];
+#pragma unroll
+        for (int cb = 0; cb < NMMA / 16; ++cb) {
+          float t[16];
+          load_d16(d_tmem, cb, t);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[cb * 16 + j] = t[j];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty(pd.idx));
+        pd.next();
+#pragma unroll
+        for (int cb = 0; cb < NMMA / 16; ++cb) {
+          if (full_tile) {
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = v[cb * 16 + j] * s;
+            E::emit16(pr, mt, nt, r, cb, o, xch);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[cb * 16 + j];
+          }
+        }
+        if (full_tile) continue;
       } else {
         const float s = E::row_scale(pr, prow);
         for (int cb = 0; cb < NMMA / 16; ++cb) {
