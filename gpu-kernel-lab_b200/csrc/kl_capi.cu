@@ -530,7 +530,7 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan");
   out[0] = 2;
   out[1] = plan.grid;
-  out[2] = tc_threads(plan.n_mma, plan.kblk);
+  out[2] = tc_threads(w_format, plan.n_mma, plan.kblk);
   out[3] = plan.smem;
   out[4] = plan.n_mma;
   out[5] = plan.w_stages;

@@ -32,7 +32,7 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& p, int fmt, bool swig
 // tile) converted to bf16/f16 into tensor memory as the MMA's A operand and X
 // (n_mma tokens per tile) TMA-staged in shared memory as the B operand.
 constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
-constexpr int kTcWarps = 15;          // W-TMA, MMA, X-TMA, 8 converter, 4 epilogue warps (+ extra MMA issuers)
+// Block composition is per kernel instantiation (TcRoles in kl_tc_gemm.cu).
 constexpr int kCounterBytes = 64 * 1024;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxGroup = 512;        // problems per grouped launch
@@ -70,7 +70,7 @@ struct TcPlan {
   size_t workspace;                   // counters + partials
 };
 int tc_choose_nmma(int m, int fmt);
-int tc_threads(int n_mma, int kblk);  // block size of the tcgen05 kernel for this token tile
+int tc_threads(int fmt, int n_mma, int kblk);  // block size of the tcgen05 kernel
 // Fill the tiling fields of a problem (m_tiles, n_tiles, kb_total) for K blocks
 // of kblk elements; returns its unit count.
 long long tc_problem_tiles(TcProblem& pr, int n_mma, int kblk, bool swiglu);

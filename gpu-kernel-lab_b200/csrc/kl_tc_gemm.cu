@@ -51,8 +51,7 @@ namespace {
 // region; the epilogue adds the NI partial accumulators.
 template <int NMMA, int KBL>
 struct TcCfg {
-  static constexpr int NI = NMMA <= 32 ? (KBL == 256 ? 2 : 4) : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
-  static constexpr int THREADS = (kTcWarps + NI - 1) * 32;
+  static constexpr int NI = NMMA <= 32 ? 4 : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
   static constexpr int ACOLS = KBL / 2;                      // TMEM columns of one A stage (bf16 pairs)
   static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D accumulator
   static constexpr int A_STAGES_FIT = (512 - 2 * NI * D_PITCH) / ACOLS;
@@ -69,15 +68,36 @@ struct TcCfg {
 };
 
 template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL_W4_ASYM; }
+
+// Warp roles: 0 W-TMA, 1 MMA issuer 0 (+ TMEM owner), 2 X-TMA, then CW
+// converter warps (CW/4 per TMEM lane quadrant, each converting a 1/(CW/4)
+// slice of the K block), 4 epilogue warps, then the NI-1 other MMA issuers,
+// then (optional) a second epilogue group that owns accumulator buffer 1 and
+// finishes every other tile.  The int -> bf16 conversion is latency-bound at
+// two warps per scheduler, so the 256-element stages with small token tiles
+// get four converter warps per scheduler.
+template <int FMT, int NMMA, int KBL>
+struct TcRoles {
+  static constexpr int NI = TcCfg<NMMA, KBL>::NI;
+  static constexpr int CW = (KBL == 256 && NMMA <= 32) ? 16 : 8;
+  static constexpr int CONV0 = 3;
+  static constexpr int EPI0_WARP0 = CONV0 + CW;
+  static constexpr int ISS1_WARP0 = EPI0_WARP0 + 4;
+  static constexpr int EPI_GROUPS = 1;
+  static constexpr int EPI1_WARP0 = ISS1_WARP0 + NI - 1;
+  static constexpr int WARPS = EPI1_WARP0 + 4 * (EPI_GROUPS - 1);
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int EPT = KBL / (CW / 4);                // K elements per converter thread and stage
+};
 // Weight stage: 128 rows x KBL elements, stored as column blocks of one
 // swizzle span (128 B of int8 / 64 B of packed int4) by 128 rows.
 template <int FMT, int KBL> constexpr int w_row_bytes() { return is_w4<FMT>() ? KBL / 2 : KBL; }
 template <int FMT, int KBL> constexpr int w_stage_bytes() { return 128 * w_row_bytes<FMT, KBL>(); }
 template <int FMT> constexpr bool grouped() { return is_w4<FMT>(); }
 
-constexpr int kXchBytes = 64 * 16 * 4;            // SwiGLU up-value exchange: 64 rows x 16 cols f32
+constexpr int kXchFloats = 64 * 16;               // SwiGLU up-value exchange: 64 rows x 16 cols f32
+constexpr int kXchBytes = 2 * kXchFloats * 4;      // one exchange area per epilogue group
 constexpr int kUnitCacheBytes = 8 * kMaxGroup;    // problem unit_begin cache (grouped launches)
-constexpr int kFirstEpiThread = 11 * 32;
 
 struct SmemLayout {
   uint32_t w, x, xch, ucache, bars, misc, total;
@@ -131,7 +151,8 @@ KL_DEVICE void drain_ring(BarFn full, int n, int issued) {
   }
 }
 
-KL_DEVICE void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier among the 4 warps of one epilogue group (ids 1 and 2; 0 is __syncthreads).
+KL_DEVICE void named_bar_epi(int g) { asm volatile("bar.sync %0, 128;" :: "r"(1 + g) : "memory"); }
 
 struct Problems {
   const TcParams* p;
@@ -215,7 +236,8 @@ struct Epi {
     }
   }
   // Emit 16 token columns [cb*16, cb*16+16) of tile row r.
-  KL_DEVICE static void emit16(const TcProblem& pr, int mt, int nt, int r, int cb, const float (&v)[16], float* xch) {
+  KL_DEVICE static void emit16(const TcProblem& pr, int mt, int nt, int r, int cb, const float (&v)[16], float* xch,
+                               int g) {
     const int m0 = mt * NMMA + cb * 16;
     if constexpr (!SWIGLU) {
       const int n = nt * 128 + r;
@@ -235,7 +257,7 @@ struct Epi {
 #pragma unroll
         for (int j = 0; j < 16; ++j) xch[(r - 64) * 16 + ((j + r) & 15)] = v[j];
       }
-      named_bar_epi();
+      named_bar_epi(g);
       if (r < 64) {
         const int n = nt * 64 + r;
         if (n < pr.n_out) {
@@ -251,15 +273,16 @@ struct Epi {
           }
         }
       }
-      named_bar_epi();
+      named_bar_epi(g);
     }
   }
 };
 
 template <int FMT, int NMMA, int KBL, bool SWIGLU, bool XBF16>
-__global__ void __launch_bounds__(TcCfg<NMMA, KBL>::THREADS, 1)
+__global__ void __launch_bounds__(TcRoles<FMT, NMMA, KBL>::THREADS, 1)
 tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   using Cfg = TcCfg<NMMA, KBL>;
+  using Roles = TcRoles<FMT, NMMA, KBL>;
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
   static_assert(!grouped<FMT>() || KBL == 128, "4-bit group mode: one group of 128 per stage");
   constexpr int WSB = w_stage_bytes<FMT, KBL>();
@@ -278,7 +301,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   long long* ucache = reinterpret_cast<long long*>(smem + L.ucache);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc + 4);
-  volatile int* fix_flag = reinterpret_cast<volatile int*>(smem + L.misc + 8);
+  volatile int* fix_flags = reinterpret_cast<volatile int*>(smem + L.misc + 8);   // one per epilogue group
   auto w_full = [&](int i) { return s_bars + 8u * i; };
   auto w_empty = [&](int i) { return s_bars + 8u * (SW + i); };
   auto x_full = [&](int i) { return s_bars + 8u * (2 * SW + i); };
@@ -319,13 +342,14 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     cw.next();
   };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), 8); }
+    for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), Roles::CW); }
     for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), Cfg::NI); }
-    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), 8); mbar_init(a_empty(i), Cfg::NI); }
+    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), Roles::CW); mbar_init(a_empty(i), Cfg::NI); }
     for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), Cfg::NI); mbar_init(d_empty(i), 4); }
     mbar_init(done_bar, Cfg::NI);
     *abort_flag = 0;
-    *fix_flag = 0;
+    fix_flags[0] = 0;
+    fix_flags[1] = 0;
     fence_mbar_init();
     cw.init(probs, u_lo, u_hi);
     if (n_local > 0) prefetch_tmap(&cw.pr->tmap_w);
@@ -379,12 +403,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       }
       if (!ok) drain_ring(x_full, SX, issued);
     }
-  } else if (warp == 1 || warp >= kTcWarps) {
+  } else if (warp == 1 || (warp >= Roles::ISS1_WARP0 && warp < Roles::EPI1_WARP0)) {
     // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
       constexpr int JPER = Cfg::KSTEPS / Cfg::NI;    // K steps of 16 per issuer and stage
-      const int w = warp == 1 ? 0 : warp - kTcWarps + 1;
+      const int w = warp == 1 ? 0 : warp - Roles::ISS1_WARP0 + 1;
       Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
       bool ok = true;
       Cursor cm;
@@ -418,10 +442,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       tc_commit(done_bar);
       mbar_wait_time(done_bar, 0);
     }
-  } else if (warp < 11) {
+  } else if (warp < Roles::EPI0_WARP0) {
     // -------------------------------------------------------------- converters
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
-    const int h = (warp - 3) >> 2;          // which half of the K block (64 elements)
+    const int h = (warp - Roles::CONV0) >> 2;   // which slice of the K block
     const int r = q * 32 + lane;            // tile row owned by this thread
     Pipe pwc{0, SW, 0}, pa{0, A, 0};
     Cursor cc_;
@@ -429,7 +453,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     for (int i = 0; i < n_local; ++i, cc_.next()) {
       if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
-      constexpr int EPT = KBL / 2;                 // elements per thread (half a stage row)
+      constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
       const uint8_t* wstage = smem + L.w + pwc.idx * WSB;
       uint32_t out[EPT / 2];
       if constexpr (!is_w4<FMT>()) {
@@ -497,8 +521,15 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    const int eg = warp >= Roles::EPI1_WARP0 ? 1 : 0;          // epilogue group
+    const int first_thread = (eg ? Roles::EPI1_WARP0 : Roles::EPI0_WARP0) * 32;
+    volatile int* fix_flag = fix_flags + eg;
+    float* xg = xch + eg * kXchFloats;
     pdl_wait();                             // outputs / workspace written only after the previous kernel
-    Pipe pd{0, 2, 0};
+    // chunk c uses accumulator buffer c % 2; with two groups, group g takes the
+    // chunks with c % 2 == g, i.e. always buffer g
+    Pipe pd{eg, 2, 0};
+    int chunk = 0;
     float acc[grouped<FMT>() ? NMMA : 1];
     int seg_kb0 = 0;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
@@ -534,6 +565,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       }
       const bool chunk_end = grouped<FMT>() ? true : seg_end;
       if (!chunk_end) continue;
+      const int my_chunk = chunk++;
+      if (Roles::EPI_GROUPS == 2 && (my_chunk & 1) != eg) continue;
       if (!(ok = wait_bar(d_full(pd.idx), pd.phase, abort_flag, p.status))) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + lane_base + Cfg::d_col(pd.idx, 0);
@@ -561,7 +594,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_empty(pd.idx));
-        pd.next();
+        if (Roles::EPI_GROUPS == 2) pd.phase ^= 1u; else pd.next();
         if (!seg_end) continue;
         if (full_tile) {
 #pragma unroll
@@ -569,7 +602,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = acc[cb * 16 + j];
-            E::emit16(pr, mt, nt, r, cb, o, xch);
+            E::emit16(pr, mt, nt, r, cb, o, xg, eg);
           }
           continue;
         }
@@ -592,14 +625,14 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_empty(pd.idx));
-        pd.next();
+        if (Roles::EPI_GROUPS == 2) pd.phase ^= 1u; else pd.next();
 #pragma unroll
         for (int cb = 0; cb < NMMA / 16; ++cb) {
           if (full_tile) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = v[cb * 16 + j] * s;
-            E::emit16(pr, mt, nt, r, cb, o, xch);
+            E::emit16(pr, mt, nt, r, cb, o, xg, eg);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[cb * 16 + j];
@@ -615,7 +648,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = v[j] * s;
-            E::emit16(pr, mt, nt, r, cb, o, xch);
+            E::emit16(pr, mt, nt, r, cb, o, xg, eg);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[j];
@@ -624,23 +657,23 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_empty(pd.idx));
-        pd.next();
+        if (Roles::EPI_GROUPS == 2) pd.phase ^= 1u; else pd.next();
         if (full_tile) continue;
       }
       // ---- split tile: publish the partial, the last contributor finishes it.
       const long long c_first = unit_owner(ce.tile_u0, p.units, G);
       const long long c_last = unit_owner(ce.tile_u0 + ce.kb_total - 1, p.units, G);
       __threadfence();
-      named_bar_epi();
-      if (threadIdx.x == kFirstEpiThread) {
+      named_bar_epi(eg);
+      if (threadIdx.x == first_thread) {
         const int old = atomicAdd(p.counters + c_first, 1);
         const int last = (old == static_cast<int>(c_last - c_first));
         if (last) p.counters[c_first] = 0;   // ready for the next launch
         *fix_flag = last;
       }
-      named_bar_epi();
+      named_bar_epi(eg);
       const bool last = *fix_flag != 0;
-      named_bar_epi();                        // everyone read fix_flag before it is reused
+      named_bar_epi(eg);                      // everyone read fix_flag before it is reused
       if (!last) continue;
       __threadfence();
       const float s = grouped<FMT>() ? 1.0f : E::row_scale(pr, prow);
@@ -661,7 +694,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] *= s;
-        E::emit16(pr, mt, nt, r, cb, o, xch);
+        E::emit16(pr, mt, nt, r, cb, o, xg, eg);
       }
     }
   }
@@ -689,7 +722,7 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(plan.grid);
-  cfg.blockDim = dim3(TcCfg<NMMA, KBL>::THREADS);
+  cfg.blockDim = dim3(TcRoles<FMT, NMMA, KBL>::THREADS);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -735,25 +768,26 @@ cudaError_t launch_fmt(const TcParams& p, const TcPlan& plan, int fmt, bool pdl,
 
 }  // namespace
 
-int tc_threads(int n_mma, int kblk) {
+int tc_threads(int fmt, int n_mma, int kblk) {
+  const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
   if (kblk == 256) {
     switch (n_mma) {
-      case 16: return TcCfg<16, 256>::THREADS;
-      case 32: return TcCfg<32, 256>::THREADS;
-      default: return TcCfg<64, 256>::THREADS;
+      case 16: return TcRoles<KL_W8_ROW, 16, 256>::THREADS;
+      case 32: return TcRoles<KL_W8_ROW, 32, 256>::THREADS;
+      default: return TcRoles<KL_W8_ROW, 64, 256>::THREADS;
     }
   }
   switch (n_mma) {
-    case 16: return TcCfg<16, 128>::THREADS;
-    case 32: return TcCfg<32, 128>::THREADS;
-    case 64: return TcCfg<64, 128>::THREADS;
-    default: return TcCfg<128, 128>::THREADS;
+    case 16: return TcRoles<KL_W8_ROW, 16, 128>::THREADS;
+    case 32: return TcRoles<KL_W8_ROW, 32, 128>::THREADS;
+    case 64: return w4 ? TcRoles<KL_W4_ASYM, 64, 128>::THREADS : TcRoles<KL_W8_ROW, 64, 128>::THREADS;
+    default: return TcRoles<KL_W8_ROW, 128, 128>::THREADS;
   }
 }
 
 static int tc_a_stages(int n_mma, int kblk) {
   if (kblk == 256) return n_mma <= 32 ? TcCfg<16, 256>::A_STAGES : TcCfg<64, 256>::A_STAGES;
-  return 4;
+  return n_mma <= 32 ? TcCfg<16, 128>::A_STAGES : (n_mma == 64 ? TcCfg<64, 128>::A_STAGES : TcCfg<128, 128>::A_STAGES);
 }
 
 int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count) {
