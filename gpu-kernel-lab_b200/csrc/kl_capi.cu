@@ -167,6 +167,15 @@ int validate_linear(const void* x, int x_dtype, int m, int k, const void* w, int
 }
 
 }  // namespace
+
+int report_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 }  // namespace kl
 
 using namespace kl;

@@ -35,6 +35,9 @@ constexpr int kTcRows = 128;          // weight rows per tile (MMA M)
 // Block composition is per kernel instantiation (TcRoles in kl_tc_gemm.cu).
 constexpr int kCounterBytes = 64 * 1024;
 constexpr int kMaxDevices = 64;
+
+// Records a formatted message for kl_last_error() and returns `code`.
+int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 constexpr int kMaxGroup = 512;        // problems per grouped launch
 constexpr int kMaxWStages = 16;
 

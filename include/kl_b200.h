@@ -87,6 +87,30 @@ int kl_linear(const void* x, int x_dtype, int m, int k,
 size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, int flags);
 
 /*
+ * kl_linear for KL_W8_ROW weights without a workspace argument.  No counterpart
+ * in the reference: it serves callers that cannot allocate device memory, such
+ * as an FFI binding handed only the model's tensors by a host runtime that owns
+ * all device allocation, or code running while another library captures a
+ * CUDA graph (cudaMalloc is not allowed then).
+ *   Arguments mean what they mean for kl_linear (w_format KL_W8_ROW, no flags).
+ *   Scratch: a file-scope device array of KL_NOALLOC_SCRATCH_BYTES inside this
+ *     library, held on every GPU that loads it until the process exits.  Enough
+ *     for m <= KL_NOALLOC_MAX_M on devices with up to 160 SMs; larger m returns
+ *     KL_ERR_INVALID, a device whose plan needs more returns KL_ERR_WORKSPACE.
+ *   The first call on each device looks up that device's scratch address; make
+ *     that first call before any stream capture.
+ *   Every call clears the scratch's arrival counters on `stream` before the
+ *     kernel.  All calls share the one array, so calls that overlap on the GPU
+ *     (two streams, two host threads) race; keep them ordered on one stream.
+ *   Allocates nothing: no cudaMalloc, no cudaFree, no allocating library call.
+ */
+#define KL_NOALLOC_MAX_M         64
+#define KL_NOALLOC_SCRATCH_BYTES (10 * 1024 * 1024 + 64 * 1024)
+int kl_linear_noalloc(const void* x, int x_dtype, int m, int k,
+                      const void* w, int n, const void* scales,
+                      int swiglu, void* y, void* stream);
+
+/*
  * Grouped launch: many independent GEMMs (same weight format, activation dtype
  * and SwiGLU mode; any shapes) streamed by ONE persistent tcgen05 kernel --
  * no launch gaps, one stream-K partition over the weights of every problem.
