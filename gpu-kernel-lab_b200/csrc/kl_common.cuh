@@ -104,6 +104,22 @@ KL_DEVICE void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
       :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// High word of a SW128 K-major shared-memory descriptor (SBO 1024 B, version 1,
+// SWIZZLE_128B); smem_desc_sw128_lo below builds the low word.
+constexpr uint32_t kSmemDescSw128Hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+// tc_mma_ts with the B descriptor given as (low word, constant high word).
+KL_DEVICE void tc_mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_desc_lo, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b64 bd;\n setp.ne.b32 p, %5, 0;\n mov.b64 bd, {%2, %3};\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n}"
+      :: "r"(d_tmem), "r"(a_tmem), "r"(b_desc_lo), "n"(kSmemDescSw128Hi), "r"(idesc), "r"(accumulate) : "memory");
+}
+// True in exactly one active lane of the warp (all lanes must call it).
+KL_DEVICE bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(pred));
+  return pred != 0;
+}
 // Arrive (once) on an mbarrier when all previously issued tcgen05 ops of this thread complete.
 KL_DEVICE void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
@@ -140,6 +156,11 @@ KL_DEVICE uint64_t smem_desc_sw128(uint32_t saddr) {
   d |= static_cast<uint64_t>(2u) << 61;                    // SWIZZLE_128B
   return d;
 }
+
+// The same descriptor split into its two 32-bit words, for issue loops that
+// only advance the start address: the address field (bits 0-13) never carries
+// into bit 14 because shared-memory addresses are below 256 KB.
+KL_DEVICE uint32_t smem_desc_sw128_lo(uint32_t saddr) { return ((saddr >> 4) & 0x3FFFu) | (1u << 16); }
 
 // Instruction descriptor, kind::f16: f32 accumulator, A and B both bf16 (or both
 // f16), both K-major, shape M x N.

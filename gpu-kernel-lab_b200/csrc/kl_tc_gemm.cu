@@ -79,7 +79,7 @@ template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL
 template <int FMT, int NMMA, int KBL>
 struct TcRoles {
   static constexpr int NI = TcCfg<NMMA, KBL>::NI;
-  static constexpr int CW = (KBL == 256 && NMMA <= 32) ? 16 : 8;
+  static constexpr int CW = (KBL == 256 && NMMA == 16) ? 16 : 8;
   static constexpr int CONV0 = 3;
   static constexpr int EPI0_WARP0 = CONV0 + CW;
   static constexpr int ISS1_WARP0 = EPI0_WARP0 + 4;
@@ -137,6 +137,12 @@ KL_DEVICE bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
       }
     }
   }
+}
+
+// wait_bar executed by every lane of a warp, with a warp-uniform result.
+KL_DEVICE bool wait_bar_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  const bool ok = wait_bar(bar, parity, abort_flag, status);
+  return __all_sync(0xFFFFFFFFu, ok);
 }
 
 // Abort path of a TMA producer: wait (time-bounded) until the last copy issued
@@ -405,10 +411,22 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     }
   } else if (warp == 1 || (warp >= Roles::ISS1_WARP0 && warp < Roles::EPI1_WARP0)) {
     // ------------------------------------------------------------ MMA issuers
-    if (lane == 0) {
+    // The whole warp runs the loop (so operands stay warp-uniform) and one
+    // elected lane issues the MMAs and commits.
+    {
       constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
       constexpr int JPER = Cfg::KSTEPS / Cfg::NI;    // K steps of 16 per issuer and stage
       const int w = warp == 1 ? 0 : warp - Roles::ISS1_WARP0 + 1;
+      // Descriptor and TMEM offsets of this issuer's K steps, computed once:
+      // the issue loop then costs one add per operand per MMA.
+      const uint32_t x_desc0 = smem_desc_sw128_lo(s_x);
+      uint32_t b_off[JPER];
+#pragma unroll
+      for (int jj = 0; jj < JPER; ++jj) {
+        const int j = w * JPER + jj;
+        b_off[jj] = static_cast<uint32_t>((j >> 2) * Cfg::X_ATOM + (j & 3) * 32) >> 4;
+      }
+      const uint32_t a_off = 8u * static_cast<uint32_t>(w * JPER);
       Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
       bool ok = true;
       Cursor cm;
@@ -416,30 +434,29 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       for (int i = 0; i < n_local && ok; ++i, cm.next()) {
         const bool chunk_start = grouped<FMT>() ? true : cm.seg_start();
         const bool chunk_end = grouped<FMT>() ? true : cm.seg_end();
-        if (chunk_start && !(ok = wait_bar(d_empty(pd.idx), pd.phase ^ 1u, abort_flag, p.status))) break;
-        if (!(ok = wait_bar(x_full(px.idx), px.phase, abort_flag, p.status))) break;
-        if (!(ok = wait_bar(a_full(pa.idx), pa.phase, abort_flag, p.status))) break;
+        if (chunk_start && !(ok = wait_bar_warp(d_empty(pd.idx), pd.phase ^ 1u, abort_flag, p.status))) break;
+        if (!(ok = wait_bar_warp(x_full(px.idx), px.phase, abort_flag, p.status))) break;
+        if (!(ok = wait_bar_warp(a_full(pa.idx), pa.phase, abort_flag, p.status))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + Cfg::d_col(pd.idx, w);
-        const uint32_t a_tmem = tmem + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx;
-        const uint32_t xs = s_x + px.idx * Cfg::X_STAGE;
+        const uint32_t a_tmem = tmem + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx + a_off;
+        const uint32_t xd = x_desc0 + static_cast<uint32_t>(px.idx * (Cfg::X_STAGE >> 4));
+        if (elect_one()) {
 #pragma unroll
-        for (int jj = 0; jj < JPER; ++jj) {
-          const int j = w * JPER + jj;
-          const uint64_t bdesc = smem_desc_sw128(xs + (j >> 2) * Cfg::X_ATOM + (j & 3) * 32);
-          tc_mma_ts(d_tmem, a_tmem + 8u * j, bdesc, idesc, (chunk_start && jj == 0) ? 0u : 1u);
+          for (int jj = 0; jj < JPER; ++jj)
+            tc_mma_ts_lo(d_tmem, a_tmem + 8u * jj, xd + b_off[jj], idesc, (chunk_start && jj == 0) ? 0u : 1u);
+          tc_commit(x_empty(px.idx));
+          tc_commit(a_empty(pa.idx));
+          if (chunk_end) tc_commit(d_full(pd.idx));
         }
-        tc_commit(x_empty(px.idx));
-        tc_commit(a_empty(pa.idx));
+        __syncwarp();
         px.next();
         pa.next();
-        if (chunk_end) {
-          tc_commit(d_full(pd.idx));
-          pd.next();
-        }
+        if (chunk_end) pd.next();
       }
       // Make sure no MMA is still reading/writing TMEM when the CTA tears down.
-      tc_commit(done_bar);
+      if (elect_one()) tc_commit(done_bar);
+      __syncwarp();
       mbar_wait_time(done_bar, 0);
     }
   } else if (warp < Roles::EPI0_WARP0) {
