@@ -115,37 +115,62 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU paths
-def cpu_path_sample(workload_shapes, m, budget_s=10.0, seed=0):
+def cpu_path_sample(workload_shapes, m_list, fmt="w8_row", budget_s=10.0, seed=0):
     """The reference's CPU path (dequantise, fp32 matmul, bf16 cast -- restated in
-    ``oracle/``) over a bounded sample of the workload's GEMMs.  Returns
-    (GB/s of algorithmic bytes, seconds, description, threads)."""
+    ``oracle/``) over a bounded sample of the workload: every GEMM shape at every
+    batch size, each on a row sample.  Returns (GB/s of algorithmic bytes,
+    seconds, description, threads)."""
     import numpy as np
     from threadpoolctl import threadpool_info
 
     from oracle import quant_oracle as O
     rng = np.random.default_rng(seed)
-    done_bytes, t_total, names = 0, 0.0, []
+    done_bytes, t_total, calls = 0, 0.0, 0
     prepared = []
     for name, n, k in workload_shapes:
         rows = min(n, 8192)            # bounded sample of rows per GEMM
         w = (rng.standard_normal((rows, k), dtype=np.float32) * 0.02)
-        q, s = O.quantize_int8_rowwise(w)
-        x = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
-        prepared.append((name, rows, k, q, s, x))
+        if fmt == "w4_asym":
+            d, sc, z = O.quantize_int4_asym(w, 128)
+            deq = (lambda d=d, sc=sc, z=z: O.dequantize_int4_asym(d, sc, z, 128))
+            wbytes = rows * k // 2 + 4 * rows * (k // 128)
+        else:
+            q, sc = O.quantize_int8_rowwise(w)
+            deq = (lambda q=q, sc=sc: O.dequantize_int8_rowwise(q, sc))
+            wbytes = rows * k + 2 * rows
+        for m in m_list:
+            x = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
+            prepared.append((deq, x, wbytes + 2 * m * k + 2 * m * rows))
     start = time.perf_counter()
     while time.perf_counter() - start < budget_s:
-        for name, rows, k, q, s, x in prepared:
+        for deq, x, nbytes in prepared:
             t0 = time.perf_counter()
-            O.linear(x, O.dequantize_int8_rowwise(q, s))
+            O.linear(x, deq())
             t_total += time.perf_counter() - t0
-            done_bytes += rows * k + 2 * rows + 2 * m * k + 2 * m * rows
-            names.append(name)
+            done_bytes += nbytes
+            calls += 1
             if time.perf_counter() - start >= budget_s:
                 break
     threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    desc = (f"M={m}: {len(names)} GEMM calls over row samples (<=8192 rows) of "
-            f"{', '.join(sorted(set(names)))}; dequantise + numpy/BLAS fp32 matmul + bf16 cast")
+    desc = (f"M in {m_list}: {calls} GEMM calls over row samples (<=8192 rows) of "
+            f"{', '.join(name for name, _, _ in workload_shapes)}; {fmt} dequantise + numpy/BLAS fp32 matmul + bf16 cast")
     return done_bytes / t_total / 1e9, t_total, desc, threads
+
+
+def workload_of(args):
+    """(GEMM shapes, batch sizes, weight format, description) of the decode workloads."""
+    if args.workload == "llama":
+        shapes, ms, fmt = LLAMA_LAYER + [LLAMA_HEAD], [1, 64, 256], "w8_row"
+        desc = "llama-3.2-3b decode projection set (BASELINE config 4)"
+    elif args.workload == "w4":
+        shapes, ms, fmt = QWEN_LAYER + [QWEN_HEAD], [1, 16], "w4_asym"
+        desc = "qwen3-0.6b decode projection set, W4A16 asym g128 (BASELINE config 3)"
+    else:
+        shapes, ms, fmt = QWEN_LAYER + [QWEN_HEAD], [1, 8, 32, 64], "w8_row"
+        desc = "qwen3-0.6b decode projection set (BASELINE config 1)"
+    if args.batch:
+        ms = [int(v) for v in args.batch.split(",")]
+    return shapes, ms, fmt, desc
 
 
 def run_reference(args):
@@ -153,11 +178,11 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    shapes = QWEN_LAYER + [QWEN_HEAD] if args.workload != "llama" else LLAMA_LAYER + [LLAMA_HEAD]
+    shapes, ms, fmt, wdesc = workload_of(args)
     per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
     vals = []
     for i in range(args.warmup + args.steps):
-        v, _, desc, threads = cpu_path_sample(shapes, 1, budget_s=per_step, seed=i)
+        v, _, desc, threads = cpu_path_sample(shapes, ms, fmt, budget_s=per_step, seed=i)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.mean(vals)
@@ -165,10 +190,10 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per_step * 1000, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "reference CPU path (dequantise + fp32 matmul) on a bounded sample, M=1",
-                       "gpus_used": 0},
+            "config": {"workload": wdesc, "batch_m": ms, "gpus_used": 0,
+                       "path": "reference CPU path (dequantise + fp32 matmul + bf16 cast), bounded row samples"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": desc},
+                             "sample": desc + f" ({per_step:.1f} s per step)"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -194,7 +219,11 @@ def init_dist(args):
     return world, rank, local, pg
 
 
-def build_weights(kl, shapes, layers, device, seed=1234):
+def quantize(kl, w, fmt):
+    return kl.quantize_int4_asym(w, 128) if fmt == "w4_asym" else kl.quantize_int8_rowwise(w)
+
+
+def build_weights(kl, shapes, layers, device, seed=1234, fmt="w8_row"):
     import torch
     gen = torch.Generator(device=device)
     weights = []
@@ -202,7 +231,7 @@ def build_weights(kl, shapes, layers, device, seed=1234):
         for j, (name, n, k) in enumerate(shapes):
             gen.manual_seed(seed + li * 16 + j)
             w = torch.randn(n, k, device=device, generator=gen) * 0.02
-            weights.append((f"{name}{li}", kl.quantize_int8_rowwise(w)))
+            weights.append((f"{name}{li}", quantize(kl, w, fmt)))
             del w
     return weights
 
@@ -215,12 +244,12 @@ def bench_decode(args, kl, world, rank, local, dist):
     import torch
     device = torch.device("cuda", local)
     layer, head = (LLAMA_LAYER, LLAMA_HEAD) if args.workload == "llama" else (QWEN_LAYER, QWEN_HEAD)
-    ms_list = [int(v) for v in args.batch.split(",")] if args.batch else ([1, 64, 256] if args.workload == "llama" else [1, 8, 32, 64])
-    weights = build_weights(kl, layer, LAYERS, device)
+    _, ms_list, fmt, workload_desc = workload_of(args)
+    weights = build_weights(kl, layer, LAYERS, device, fmt=fmt)
     gen = torch.Generator(device=device)
     gen.manual_seed(4321)
     hw = torch.randn(head[1], head[2], device=device, generator=gen) * 0.02
-    weights.append(("lm_head", kl.quantize_int8_rowwise(hw)))
+    weights.append(("lm_head", quantize(kl, hw, fmt)))
     del hw
     torch.cuda.empty_cache()
 
@@ -230,15 +259,15 @@ def bench_decode(args, kl, world, rank, local, dist):
     for m in ms_list:
         items = []
         for name, p in weights:
-            n, k = p.data.shape
+            n, k = p.shape
             x = torch.randn(m, k, device=device, generator=xg).to(torch.bfloat16)
             y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
             items.append((name, p, x, y))
         passes[m] = items
 
     def pass_bytes(m):
-        return sum(p.data.shape[0] * p.data.shape[1] + 2 * p.data.shape[0] + 2 * m * p.data.shape[1]
-                   + 2 * m * p.data.shape[0] for _, p, _, _ in passes[m])
+        # weights + their scales (and zeros) + activations in + outputs
+        return sum(p.storage_bytes + 2 * m * x.shape[1] + 2 * m * y.shape[1] for _, p, x, y in passes[m])
 
     grouped = {m: kl.GroupedLinear([(x, p, y) for _, p, x, y in passes[m]]) for m in ms_list}
 
@@ -344,19 +373,53 @@ def bench_decode(args, kl, world, rank, local, dist):
     name, p, x, y = passes[ms_list[0]][-1]
     head_graph = capture(lambda: [kl.quant_linear(x, p, out=y, pdl=True) for _ in range(5)])
     head_ms = timed(head_graph, 4) / 5
-    n, k = p.data.shape
+    n, k = p.shape
     m0 = ms_list[0]
-    head_gbs = (n * k + 2 * n + 2 * m0 * k + 2 * m0 * n) / (head_ms * 1e-3) / 1e9
+    head_gbs = (p.storage_bytes + 2 * m0 * k + 2 * m0 * n) / (head_ms * 1e-3) / 1e9
+
+    # ---- vocab-sharded lm_head + NCCL all-gather of the logits (N > 1)
+    sharded = None
+    if world > 1 or args.lm_head_shard:
+        full = passes[ms_list[0]][-1][1]
+        vocab = full.shape[0]
+        lo, hi = kl.sharded_head.shard_bounds(vocab, world, rank)
+        if fmt == "w4_asym":
+            shard = kl.PackedInt4Asym(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous(),
+                                      full.zeros[lo:hi].contiguous(), full.group_size)
+        else:
+            shard = kl.RowwiseInt8(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous())
+        shead = kl.VocabShardedHead(shard, vocab)
+        sharded = {"vocab": vocab, "ranks": world, "rows_per_rank": hi - lo, "per_m": {}}
+        for m in ms_list:
+            x = passes[m][-1][2]
+            gathered = torch.empty(vocab, m, dtype=torch.bfloat16, device=device)
+            for _ in range(3):
+                shead(x, gathered=gathered)
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = max(5, args.steps)
+            a.record()
+            for _ in range(reps):
+                shead(x, gathered=gathered)
+            b.record()
+            barrier()
+            t = a.elapsed_time(b) / reps
+            if dist is not None:
+                tt = torch.tensor([t], device=device)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                t = tt.item()
+            sharded["per_m"][str(m)] = {"ms": round(t, 4), "allgather_bytes": vocab * m * 2,
+                                        "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1)}
 
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": ("llama-3.2-3b" if args.workload == "llama" else "qwen3-0.6b") +
-                               " decode projection set (BASELINE config " + ("4" if args.workload == "llama" else "1") + ")",
+        "config": {"workload": workload_desc,
                    "batch_m": ms_list, "gemms_per_pass": len(passes[ms_list[0]]),
-                   "bytes_per_step": step_bytes, "weights": "int8 per-row bf16 scale, N(0,0.02) seeded",
+                   "bytes_per_step": step_bytes, "weights": ("4-bit asym, bf16 scale/zero per 128-group" if fmt == "w4_asym" else "int8 per-row bf16 scale")
+                              + ", N(0,0.02) seeded",
                    "l2": "inputs larger than L2: each pass streams >=0.6 GB of weights, no flush needed",
                    "parallelism": f"replicas x{world}",
                    "launch": "one grouped tcgen05 launch per M (113 independent GEMMs), CUDA graph"},
@@ -369,6 +432,7 @@ def bench_decode(args, kl, world, rank, local, dist):
                                        "frac": round(head_gbs / hbm, 3), "m": m0}},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 4)},
+        "lm_head_sharded": sharded,
         "gpu_launches": len(ms_list) * args.steps,
         "clocks": clocks.summary(),
     }
@@ -432,7 +496,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "llama", "w4"], default="decode")
     ap.add_argument("--batch", default="", help="comma-separated M values (overrides the workload's)")
     ap.add_argument("--swiglu", action="store_true", help="prefill: fuse SwiGLU into gate_up")
     ap.add_argument("--lm-head-shard", action="store_true", help="llama: vocab-shard the lm_head + NCCL all-gather")
@@ -450,8 +514,8 @@ def main():
         else:
             result = bench_decode(args, kl, world, rank, local, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "prefill":
-            shapes = QWEN_LAYER + [QWEN_HEAD] if args.workload != "llama" else LLAMA_LAYER + [LLAMA_HEAD]
-            v, secs, desc, threads = cpu_path_sample(shapes, 1, budget_s=10.0)
+            shapes, ms, fmt, _ = workload_of(args)
+            v, secs, desc, threads = cpu_path_sample(shapes, ms, fmt, budget_s=10.0)
             result["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                       "sample": desc + f" ({secs:.1f} s)"}
         elif rank == 0 and world == 1 and not args.no_cpu_baseline:

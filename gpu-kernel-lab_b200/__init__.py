@@ -10,7 +10,7 @@ kernels in ``libkl_b200.so`` (C ABI: ``include/kl_b200.h``).
 The directory name contains hyphens, so import it with
 ``importlib.import_module("gpu-kernel-lab_b200")``.
 """
-from . import _native, kernel_policy
+from . import _native, kernel_policy, sharded_head
 from .activation_int8 import (CalibratedInt8, RowwiseInt8, dequantize_int8, dequantize_int8_rowwise,
                               quantize_int8, quantize_int8_rowwise)
 from .cuda_decode import extension, project
@@ -20,6 +20,7 @@ from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequanti
                            quantize_int4_asym)
 from .native_ops import dequantize_native
 from .adapters import install_quantized_projections
+from .sharded_head import VocabShardedHead
 from .kernel_policy import QwenKernelPolicy, load_qwen_policy, select_qwen_policy
 
 __all__ = [
@@ -28,5 +29,5 @@ __all__ = [
     "quantize_int4", "dequantize_int4", "quantize_int4_asym", "dequantize_int4_asym",
     "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec", "GroupedLinear",
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
-    "select_qwen_policy",
+    "select_qwen_policy", "sharded_head", "VocabShardedHead",
 ]
