@@ -106,6 +106,11 @@ bool tc_shape_ok(int k, int w_format, int group) {
   return false;
 }
 
+// Whether the CTA-pair prefill kernel takes an (already tcgen05-eligible) problem.
+bool prefill_applies(int m, int k, int w_format, int sm_count) {
+  return w_format == KL_W8_ROW && m >= kPrefillMinM && k % prefill_k_block() == 0 && sm_count >= 2;
+}
+
 // Fill one tcgen05 problem (tensor maps + fields); the caller sets unit_begin.
 int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n,
                   const void* scales, const void* zeros, int swiglu, void* y, bool transposed, long long ldy,
@@ -235,6 +240,29 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
                 group, di.major, di.minor);
   if (!sm100) return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
   const size_t eb = act_bytes(x_dtype);
+
+  if (tc && prefill_applies(m, k, w_format, di.sm_count)) {
+    PfParams p;
+    std::memset(&p, 0, sizeof(p));
+    rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != KL_OK) return rc;
+    rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m,
+                   static_cast<uint64_t>(k) * eb, 64, 96, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != KL_OK) return rc;
+    p.scales = scales;
+    p.y = y;
+    p.ldy = transposed ? m : n_out;
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.n_out = n_out;
+    p.y_transposed = transposed ? 1 : 0;
+    p.status = di.status;
+    prefill_tiles(p, swiglu != 0);
+    const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 pair GEMM launch");
+    return KL_OK;
+  }
 
   if (tc) {
     const int mchunk = is_w4(w_format) ? 64 : m;
@@ -523,6 +551,26 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     out[1] = gp.grid_x * gp.grid_y;
     out[2] = gp.threads;
     out[3] = gp.smem;
+    return KL_OK;
+  }
+  if (prefill_applies(m, k, w_format, sm_count)) {
+    PfParams pf;
+    std::memset(&pf, 0, sizeof(pf));
+    pf.m = m;
+    pf.n = n;
+    pf.k = k;
+    pf.n_out = swiglu ? n / 2 : n;
+    prefill_tiles(pf, swiglu != 0);
+    out[0] = 3;
+    out[1] = prefill_grid(pf, sm_count);
+    out[2] = prefill_threads();
+    out[3] = prefill_smem_bytes();
+    out[4] = 192;                       // tokens per tile (pair MMA N)
+    out[5] = 8;                         // weight stages
+    out[6] = pf.n_tiles * pf.m_tiles;
+    out[7] = pf.n_tiles * pf.m_tiles * pf.kb_total;
+    if (out[1] % 2 || out[1] > (sm_count & ~1) || out[3] > 227 * 1024)
+      return fail(KL_ERR_INVALID, "pair plan out of range");
     return KL_OK;
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;

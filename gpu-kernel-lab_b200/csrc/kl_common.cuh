@@ -114,6 +114,66 @@ KL_DEVICE void tc_mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_desc_lo
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n}"
       :: "r"(d_tmem), "r"(a_tmem), "r"(b_desc_lo), "n"(kSmemDescSw128Hi), "r"(idesc), "r"(accumulate) : "memory");
 }
+// ------------------------------------------------ CTA pairs (cta_group::2)
+// A 2-CTA cluster whose tensor cores run one MMA over both CTAs' operands.
+KL_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+KL_DEVICE uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+// Arrive on an mbarrier that may live in another CTA of the cluster.
+KL_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+KL_DEVICE bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// All threads of all CTAs of the cluster (start-up / teardown only).
+KL_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+KL_DEVICE void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst_smem), "r"(ncols) : "memory");
+}
+KL_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+KL_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc] over the CTA pair (M = 256: 128 rows of
+// A and D in each CTA; B split along N between the two CTAs' shared memory).
+KL_DEVICE void tc_mma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_desc_lo, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b64 bd;\n setp.ne.b32 p, %5, 0;\n mov.b64 bd, {%2, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %4, {%6, %6, %6, %6, %6, %6, %6, %6}, p;\n}"
+      :: "r"(d_tmem), "r"(a_tmem), "r"(b_desc_lo), "n"(kSmemDescSw128Hi), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// Arrive once on the mbarrier at the same offset in every CTA of `mask` when the
+// pair's previously issued MMAs complete.
+KL_DEVICE void tc_commit_pair_mc(uint32_t bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               :: "r"(bar), "h"(mask) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier of the pair's leader CTA (`bar` is a cluster address).
+KL_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
 // True in exactly one active lane of the warp (all lanes must call it).
 KL_DEVICE bool elect_one() {
   uint32_t pred;

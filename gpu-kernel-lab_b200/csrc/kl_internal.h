@@ -83,6 +83,26 @@ int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count);
 TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count);
 cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
+// ---- prefill: int8 row-scale GEMM on CTA pairs (kl_tc_prefill.cu)
+constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel
+struct PfParams {
+  CUtensorMap tmap_w;                 // int8 [N, K], box 64 x 64 rows, 64B swizzle
+  CUtensorMap tmap_x;                 // bf16/f16 [M, K], box 64 x 96 rows, 128B swizzle
+  const void* scales;                 // bf16 [N]
+  void* y;
+  long long ldy;
+  int m, n, k, n_out;
+  int n_tiles, m_tiles, kb_total;
+  int y_transposed;
+  int* status;
+};
+int prefill_threads();
+int prefill_smem_bytes();
+int prefill_k_block();
+void prefill_tiles(PfParams& p, bool swiglu);
+int prefill_grid(const PfParams& p, int sm_count);
+cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, cudaStream_t s);
+
 // Work partition shared by the kernel and the host-side self-check:
 // CTA c owns units [lo(c), lo(c+1)) with lo(c) = floor(c * units / grid).
 __host__ __device__ inline long long unit_lo(long long c, long long units, long long grid) {

@@ -1,0 +1,394 @@
+// Prefill (many-token) int8 row-scale linear on CTA pairs:
+//   y[m, n] = s[n] * sum_k q[n, k] * x[m, k]      (optionally SwiGLU-fused)
+//
+// Each 2-CTA cluster computes a tile of 256 weight rows x 192 tokens with one
+// tcgen05 MMA stream of shape M = 256 (128 weight rows per CTA) x N = 192
+// (tokens; 96 in each CTA's shared memory) x K = 16:
+//   * every CTA converts ITS 128 weight rows of a 64-wide K block from int8 to
+//     bf16 (exact) into its own TMEM: the MMA's A operand;
+//   * every CTA loads ITS 96 tokens of the block with TMA: half of the B
+//     operand; both halves complete on the leader CTA's barrier;
+//   * the leader issues the pair's MMAs; the f32 accumulators (2 buffers of
+//     192 columns) live in each CTA's TMEM for its 128 rows;
+//   * 4 epilogue warps per CTA apply the row scale (and SwiGLU), round to the
+//     activation type and store.
+// Per SM and K block this moves 8 KB of weights and 12 KB of tokens into
+// shared memory for 3.1 MFLOP, against 16 KB + 16 KB per 2.1 MFLOP for a
+// single-CTA 128 x 128 tile: the pair halves both the shared-memory traffic
+// and the conversion work per FLOP.
+//
+// Warp roles (15 warps per CTA): 0 weight TMA, 1 token TMA, 2 TMEM owner and
+// (leader) MMA issuer, 3-10 converters (two per TMEM lane quadrant, each one
+// half of the K block), 11-14 epilogue.  Cross-CTA signalling uses mbarriers
+// only; every wait is bounded (kWaitLimitNs) and records KL_ERR_TIMEOUT.
+#include <cuda.h>
+
+#include "kl_common.cuh"
+#include "kl_internal.h"
+
+namespace kl {
+namespace {
+
+constexpr int kPfKb = 64;                        // K elements per stage
+constexpr int kPfRows = 128;                     // weight rows per CTA
+constexpr int kPfTokens = 192;                   // tokens per tile (MMA N)
+constexpr int kPfHalf = kPfTokens / 2;           // tokens per CTA
+constexpr int kPfW = 8;                          // weight stages
+constexpr int kPfX = 4;                          // token stages
+constexpr int kPfA = 4;                          // TMEM A stages
+constexpr int kPfWStage = kPfRows * kPfKb;       // 8 KB of int8
+constexpr int kPfXStage = kPfHalf * kPfKb * 2;   // 12 KB of bf16
+constexpr int kPfACols = kPfKb / 2;              // TMEM columns per A stage
+constexpr int kPfDCol0 = kPfA * kPfACols;        // 128
+constexpr int kPfConv = 8;
+constexpr int kPfEpi0 = 3 + kPfConv;
+constexpr int kPfThreads = (kPfEpi0 + 4) * 32;   // 480
+constexpr int kPfXchFloats = 64 * 16;            // SwiGLU up values of one 16-token chunk
+static_assert(kPfDCol0 + 2 * kPfTokens == 512, "TMEM budget");
+
+struct PfLayout {
+  uint32_t w, x, xch, bars, misc, total;
+};
+constexpr PfLayout pf_layout() {
+  PfLayout l{};
+  l.w = 0;
+  l.x = l.w + kPfW * kPfWStage;
+  l.xch = l.x + kPfX * kPfXStage;
+  l.bars = l.xch + kPfXchFloats * 4;
+  // w_full, w_empty [W]; x_full, x_empty [X]; a_full, a_empty [A]; d_full, d_empty [2]; done
+  l.misc = l.bars + 8 * (2 * kPfW + 2 * kPfX + 2 * kPfA + 5);
+  l.total = l.misc + 16 + 1024;
+  return l;
+}
+
+struct PfPipe {
+  int idx, n;
+  uint32_t phase;
+  KL_DEVICE void next() {
+    if (++idx == n) { idx = 0; phase ^= 1u; }
+  }
+};
+
+// Bounded wait on a local barrier that remote CTAs may arrive on (acquire at
+// cluster scope).  Returns false after the limit; records the timeout.
+KL_DEVICE bool pf_wait(uint32_t bar, uint32_t parity, int* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((spin & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+      record_error(status, KL_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+KL_DEVICE bool pf_wait_warp(uint32_t bar, uint32_t parity, int* status) {
+  return __all_sync(0xFFFFFFFFu, pf_wait(bar, parity, status));
+}
+
+template <bool SWIGLU, bool XBF16>
+__global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_constant__ PfParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr PfLayout L = pf_layout();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int tiles = p.n_tiles * p.m_tiles;
+  const int kbs = p.kb_total;
+  int my_tiles = 0;
+  if (pair < tiles) my_tiles = (tiles - 1 - pair) / pairs + 1;
+
+  const uint32_t s_w = smem_u32(smem + L.w), s_x = smem_u32(smem + L.x);
+  const uint32_t bars = smem_u32(smem + L.bars);
+  auto w_full = [&](int i) { return bars + 8u * i; };
+  auto w_empty = [&](int i) { return bars + 8u * (kPfW + i); };
+  auto x_full = [&](int i) { return bars + 8u * (2 * kPfW + i); };
+  auto x_empty = [&](int i) { return bars + 8u * (2 * kPfW + kPfX + i); };
+  auto a_full = [&](int i) { return bars + 8u * (2 * kPfW + 2 * kPfX + i); };
+  auto a_empty = [&](int i) { return bars + 8u * (2 * kPfW + 2 * kPfX + kPfA + i); };
+  auto d_full = [&](int i) { return bars + 8u * (2 * kPfW + 2 * kPfX + 2 * kPfA + i); };
+  auto d_empty = [&](int i) { return bars + 8u * (2 * kPfW + 2 * kPfX + 2 * kPfA + 2 + i); };
+  const uint32_t done_bar = bars + 8u * (2 * kPfW + 2 * kPfX + 2 * kPfA + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
+  float* xch = reinterpret_cast<float*>(smem + L.xch);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPfW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), kPfConv); }
+    for (int i = 0; i < kPfX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), 1); }
+    for (int i = 0; i < kPfA; ++i) { mbar_init(a_full(i), 2 * kPfConv); mbar_init(a_empty(i), 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), 1); mbar_init(d_empty(i), 8); }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(tmem_holder), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();                              // barrier inits and TMEM allocation visible to the pair
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- weight TMA
+    if (lane == 0 && my_tiles > 0) {
+      prefetch_tmap(&p.tmap_w);
+      PfPipe pw{0, kPfW, 0};
+      for (int it = 0; it < my_tiles; ++it) {
+        const int t = pair + it * pairs;
+        const int nt = t % p.n_tiles;
+        const int y0 = SWIGLU ? nt * 128 + static_cast<int>(rank) * 64 : nt * 256 + static_cast<int>(rank) * 128;
+        const int y1 = SWIGLU ? p.n_out + y0 : y0 + 64;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!pf_wait(w_empty(pw.idx), pw.phase ^ 1u, p.status)) { it = my_tiles; break; }
+          const uint32_t dst = s_w + pw.idx * kPfWStage;
+          mbar_arrive_expect_tx(w_full(pw.idx), kPfWStage);
+          tma_load_2d(dst, &p.tmap_w, kb * kPfKb, y0, w_full(pw.idx));
+          tma_load_2d(dst + kPfWStage / 2, &p.tmap_w, kb * kPfKb, y1, w_full(pw.idx));
+          pw.next();
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- token TMA
+    if (lane == 0 && my_tiles > 0) {
+      prefetch_tmap(&p.tmap_x);
+      const uint32_t lead_full0 = mapa_shared(x_full(0), 0);
+      PfPipe px{0, kPfX, 0};
+      for (int it = 0; it < my_tiles; ++it) {
+        const int t = pair + it * pairs;
+        const int mt = t / p.n_tiles;
+        const int row = mt * kPfTokens + static_cast<int>(rank) * kPfHalf;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!pf_wait(x_empty(px.idx), px.phase ^ 1u, p.status)) { it = my_tiles; break; }
+          if (leader) mbar_arrive_expect_tx(x_full(px.idx), 2 * kPfXStage);
+          tma_load_2d_pair(s_x + px.idx * kPfXStage, &p.tmap_x, kb * kPfKb, row, lead_full0 + 8u * px.idx);
+          px.next();
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------- MMA issuer (leader)
+    if (leader) {
+      constexpr uint32_t idesc = make_idesc_f16(256, kPfTokens, XBF16);
+      const uint32_t x_desc0 = smem_desc_sw128_lo(s_x);
+      PfPipe px{0, kPfX, 0}, pa{0, kPfA, 0}, pd{0, 2, 0};
+      bool ok = true;
+      for (int it = 0; it < my_tiles && ok; ++it) {
+        if (!(ok = pf_wait_warp(d_empty(pd.idx), pd.phase ^ 1u, p.status))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + kPfDCol0 + pd.idx * kPfTokens;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!(ok = pf_wait_warp(x_full(px.idx), px.phase, p.status))) break;
+          if (!(ok = pf_wait_warp(a_full(pa.idx), pa.phase, p.status))) break;
+          tc_fence_after();
+          const uint32_t a_tmem = tmem + pa.idx * kPfACols;
+          const uint32_t xd = x_desc0 + static_cast<uint32_t>(px.idx * (kPfXStage >> 4));
+          if (elect_one()) {
+#pragma unroll
+            for (int j = 0; j < kPfKb / 16; ++j)
+              tc_mma_pair_ts(d_tmem, a_tmem + 8u * j, xd + 2u * j, idesc, (kb == 0 && j == 0) ? 0u : 1u);
+            tc_commit_pair_mc(x_empty(px.idx), 0x3);
+            tc_commit_pair_mc(a_empty(pa.idx), 0x3);
+            if (kb == kbs - 1) tc_commit_pair_mc(d_full(pd.idx), 0x3);
+          }
+          __syncwarp();
+          px.next();
+          pa.next();
+        }
+        pd.next();
+      }
+      if (elect_one()) tc_commit_pair_mc(done_bar, 0x3);
+      __syncwarp();
+    }
+  } else if (warp < kPfEpi0) {
+    // ----------------------------------------------------------- converters
+    const int q = warp & 3;
+    const int h = (warp - 3) >> 2;             // which 32-wide half of the K block
+    const int r = q * 32 + lane;               // weight row of this CTA's 128
+    const uint32_t lead_a_full0 = mapa_shared(a_full(0), 0);
+    PfPipe pw{0, kPfW, 0}, pa{0, kPfA, 0};
+    for (int it = 0; it < my_tiles; ++it) {
+      bool ok = true;
+      for (int kb = 0; kb < kbs; ++kb) {
+        if (!(ok = pf_wait(w_full(pw.idx), pw.phase, p.status))) break;
+        if (!(ok = pf_wait(a_empty(pa.idx), pa.phase ^ 1u, p.status))) break;
+        tc_fence_after();
+        const uint8_t* ws = smem + L.w + pw.idx * kPfWStage;
+        uint32_t part[16];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int g = 2 * h + c;             // 16-byte chunk of the 64-byte row (64B swizzle)
+          const uint4 v = *reinterpret_cast<const uint4*>(ws + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+          const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int t4 = 0; t4 < 4; ++t4) {
+            if constexpr (XBF16) s8x4_to_bf16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
+            else s8x4_to_f16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
+          }
+        }
+        tmem_st16(tmem + (static_cast<uint32_t>(q * 32) << 16) + pa.idx * kPfACols + 16u * h, part);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_cluster(lead_a_full0 + 8u * pa.idx);
+          mbar_arrive(w_empty(pw.idx));
+        }
+        pw.next();
+        pa.next();
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;               // weight row of this CTA's 128
+    const uint32_t lead_d_empty0 = mapa_shared(d_empty(0), 0);
+    PfPipe pd{0, 2, 0};
+    for (int it = 0; it < my_tiles; ++it) {
+      const int t = pair + it * pairs;
+      const int nt = t % p.n_tiles, mt = t / p.n_tiles;
+      // the 4 epilogue warps take the same decision (they share named barriers)
+      const bool got = pf_wait(d_full(pd.idx), pd.phase, p.status);
+      uint32_t all_got;
+      asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 2, 128, q;\n selp.u32 %0, 1, 0, p;\n}"
+                   : "=r"(all_got) : "r"(got ? 1u : 0u) : "memory");
+      if (!all_got) break;
+      tc_fence_after();
+      // output column of this thread's row (gate rows for SwiGLU)
+      int col, wrow;
+      if constexpr (SWIGLU) {
+        col = nt * 128 + static_cast<int>(rank) * 64 + (r & 63);
+        wrow = r < 64 ? col : p.n_out + col;
+      } else {
+        col = nt * 256 + static_cast<int>(rank) * 128 + r;
+        wrow = col;
+      }
+      const bool row_ok = SWIGLU ? col < p.n_out : col < p.n;
+      const float s = row_ok ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[wrow]) : 0.0f;
+      const int m0 = mt * kPfTokens;
+      const uint32_t d_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + kPfDCol0 + pd.idx * kPfTokens;
+#pragma unroll 1
+      for (int c = 0; c < kPfTokens / 16; ++c) {
+        uint32_t raw[16];
+        tmem_ld16(d_tmem + 16u * c, raw);
+        tc_wait_ld();
+        if (c == kPfTokens / 16 - 1) {
+          // accumulator buffer fully read: release it to the leader's MMA
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(lead_d_empty0 + 8u * pd.idx);
+        }
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(raw[j]) * s;
+        if constexpr (SWIGLU) {
+          asm volatile("bar.sync 1, 128;" ::: "memory");        // previous chunk's reads done
+          if (r >= 64) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xch[(r - 64) * 16 + j] = v[j];
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (r < 64 && row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = m0 + c * 16 + j;
+              if (m < p.m) {
+                const float o = swiglu_model_ordered<XBF16>(v[j], xch[r * 16 + j]);
+                store_act<XBF16>(p.y, p.y_transposed ? static_cast<long long>(col) * p.ldy + m
+                                                     : static_cast<long long>(m) * p.ldy + col, o);
+              }
+            }
+          }
+        } else if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c * 16 + j;
+            if (m < p.m)
+              store_act<XBF16>(p.y, p.y_transposed ? static_cast<long long>(col) * p.ldy + m
+                                                   : static_cast<long long>(m) * p.ldy + col, v[j]);
+          }
+        }
+      }
+      pd.next();
+    }
+  }
+
+  // ---- teardown: every MMA of the pair has completed before TMEM is freed
+  if (warp == 2) {
+    if (my_tiles > 0 && !mbar_wait_time(done_bar, 0)) record_error(p.status, KL_ERR_TIMEOUT);
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 2) tmem_dealloc_pair(tmem, 512);
+}
+
+template <bool SWIGLU, bool XBF16>
+cudaError_t launch_pf(const PfParams& p, int grid, cudaStream_t s) {
+  auto kern = tc_prefill_kernel<SWIGLU, XBF16>;
+  constexpr int smem = static_cast<int>(pf_layout().total);
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevices && !attr[dev]) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  // no more pairs than can be resident at once (a GPC with an odd number of
+  // SMs holds fewer 2-CTA clusters than SMs / 2)
+  static int max_pairs[kMaxDevices] = {};
+  if (dev >= 0 && dev < kMaxDevices) {
+    if (max_pairs[dev] == 0) {
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = grid / 2;
+      }
+      max_pairs[dev] = n;
+    }
+    if (grid / 2 > max_pairs[dev]) cfg.gridDim = dim3(static_cast<unsigned>(2 * max_pairs[dev]));
+  }
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+}  // namespace
+
+int prefill_threads() { return kPfThreads; }
+int prefill_smem_bytes() { return static_cast<int>(pf_layout().total); }
+int prefill_k_block() { return kPfKb; }
+
+void prefill_tiles(PfParams& p, bool swiglu) {
+  p.n_tiles = swiglu ? (p.n_out + 127) / 128 : (p.n + 255) / 256;
+  p.m_tiles = (p.m + kPfTokens - 1) / kPfTokens;
+  p.kb_total = p.k / kPfKb;
+}
+
+int prefill_grid(const PfParams& p, int sm_count) {
+  const int tiles = p.n_tiles * p.m_tiles;
+  const int pairs = std::max(1, std::min(tiles, sm_count / 2));
+  return 2 * pairs;
+}
+
+cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, cudaStream_t s) {
+  if (swiglu) return xbf16 ? launch_pf<true, true>(p, grid, s) : launch_pf<true, false>(p, grid, s);
+  return xbf16 ? launch_pf<false, true>(p, grid, s) : launch_pf<false, false>(p, grid, s);
+}
+
+}  // namespace kl

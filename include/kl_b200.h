@@ -197,8 +197,9 @@ int kl_version(void);
  * with `sm_count` SMs, and a self-check of its work partition (every
  * (tile, k-block) unit covered exactly once, workspace slots in bounds).
  * Needs no GPU.  Returns KL_OK and fills `out` (array of 8 ints:
- * kernel (0 none, 1 simt, 2 tcgen05), grid, threads, smem bytes,
- * n_mma (tcgen05 token tile), stages, tiles, units).
+ * kernel, grid, threads, smem bytes,
+ * n_mma (tcgen05 token tile), stages, tiles, units); kernel 1 = CUDA-core GEMV,
+ * 2 = tcgen05 stream-K GEMM, 3 = tcgen05 CTA-pair prefill GEMM (int8 row scale, M >= 256).
  */
 int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags,
                      int sm_count, int* out);

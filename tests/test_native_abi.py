@@ -57,19 +57,26 @@ def test_validation_needs_no_gpu(kl):
 @pytest.mark.parametrize("n,k", QWEN + LLAMA)
 def test_plan_partition_w8(kl, m, n, k):
     plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, sm_count=148)
-    assert plan["kernel"] == 2
+    # M >= 256 with K a multiple of 64 runs on the CTA-pair prefill kernel
+    assert plan["kernel"] == (3 if m >= 256 and k % 64 == 0 else 2)
     assert 1 <= plan["grid"] <= 148
     assert plan["smem"] <= 227 * 1024
-    assert plan["n_mma"] in (16, 32, 64, 128)
+    assert plan["n_mma"] in (16, 32, 64, 128, 192)
     if m <= 64:
         assert plan["stages"] >= 3          # weight ring of >= 3 stages (16-32 KB each) per SM
+    if plan["kernel"] == 3:
+        assert plan["grid"] % 2 == 0 and plan["n_mma"] == 192
+        assert plan["tiles"] == ((n + 255) // 256) * ((m + 191) // 192)
 
 
-@pytest.mark.parametrize("m", [1, 16, 64])
+@pytest.mark.parametrize("m", [1, 16, 64, 512, 8192])
 @pytest.mark.parametrize("n,k", [(6144, 1024), (12288, 1024), (16384, 3072)])
 def test_plan_partition_swiglu(kl, m, n, k):
     plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, swiglu=True, sm_count=148)
-    assert plan["kernel"] == 2 and plan["tiles"] == ((n // 2 + 63) // 64) * ((m + plan["n_mma"] - 1) // plan["n_mma"])
+    if m >= 256:
+        assert plan["kernel"] == 3 and plan["tiles"] == ((n // 2 + 127) // 128) * ((m + 191) // 192)
+    else:
+        assert plan["kernel"] == 2 and plan["tiles"] == ((n // 2 + 63) // 64) * ((m + plan["n_mma"] - 1) // plan["n_mma"])
 
 
 @pytest.mark.parametrize("m", [1, 16, 200])
