@@ -257,6 +257,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     p.k = k;
     p.n_out = n_out;
     p.y_transposed = transposed ? 1 : 0;
+    p.vec_store = (!transposed && aligned16(y) && p.ldy % 8 == 0) ? 1 : 0;
     p.status = di.status;
     prefill_tiles(p, swiglu != 0);
     const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, s);

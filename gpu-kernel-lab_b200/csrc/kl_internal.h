@@ -94,6 +94,7 @@ struct PfParams {
   int m, n, k, n_out;
   int n_tiles, m_tiles, kb_total;
   int y_transposed;
+  int vec_store;                      // row-major y, 16-byte aligned, ldy % 8 == 0: 16-byte stores
   int* status;
 };
 int prefill_threads();

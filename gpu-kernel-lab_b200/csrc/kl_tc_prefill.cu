@@ -34,7 +34,7 @@ constexpr int kPfRows = 128;                     // weight rows per CTA
 constexpr int kPfTokens = 192;                   // tokens per tile (MMA N)
 constexpr int kPfHalf = kPfTokens / 2;           // tokens per CTA
 constexpr int kPfW = 8;                          // weight stages
-constexpr int kPfX = 4;                          // token stages
+constexpr int kPfX = 8;                          // token stages
 constexpr int kPfA = 4;                          // TMEM A stages
 constexpr int kPfWStage = kPfRows * kPfKb;       // 8 KB of int8
 constexpr int kPfXStage = kPfHalf * kPfKb * 2;   // 12 KB of bf16
@@ -43,18 +43,22 @@ constexpr int kPfDCol0 = kPfA * kPfACols;        // 128
 constexpr int kPfConv = 8;
 constexpr int kPfEpi0 = 3 + kPfConv;
 constexpr int kPfThreads = (kPfEpi0 + 4) * 32;   // 480
-constexpr int kPfXchFloats = 64 * 16;            // SwiGLU up values of one 16-token chunk
+constexpr int kPfChunk = 32;                     // tokens per epilogue step
+constexpr int kPfXchHalf = 64 * (kPfChunk / 2 + 1);  // one direction of the SwiGLU exchange (padded rows)
+constexpr int kPfXchFloats = 2 * kPfXchHalf;
+constexpr int kPfStageBytes = 32 * kPfChunk * 2; // per epilogue warp: 32 rows x 32 tokens, bf16
 static_assert(kPfDCol0 + 2 * kPfTokens == 512, "TMEM budget");
 
 struct PfLayout {
-  uint32_t w, x, xch, bars, misc, total;
+  uint32_t w, x, xch, stage, bars, misc, total;
 };
 constexpr PfLayout pf_layout() {
   PfLayout l{};
   l.w = 0;
   l.x = l.w + kPfW * kPfWStage;
   l.xch = l.x + kPfX * kPfXStage;
-  l.bars = l.xch + kPfXchFloats * 4;
+  l.stage = l.xch + kPfXchFloats * 4;
+  l.bars = l.stage + 4 * kPfStageBytes;
   // w_full, w_empty [W]; x_full, x_empty [X]; a_full, a_empty [A]; d_full, d_empty [2]; done
   l.misc = l.bars + 8 * (2 * kPfW + 2 * kPfX + 2 * kPfA + 5);
   l.total = l.misc + 16 + 1024;
@@ -84,6 +88,38 @@ KL_DEVICE bool pf_wait(uint32_t bar, uint32_t parity, int* status) {
 }
 KL_DEVICE bool pf_wait_warp(uint32_t bar, uint32_t parity, int* status) {
   return __all_sync(0xFFFFFFFFu, pf_wait(bar, parity, status));
+}
+
+// Store one epilogue step of one warp: output columns col0 .. col0+31 (lane =
+// column) for tokens m0 .. m0+31 (o[j] = token m0 + j).  A block that is fully
+// in range in a row-major output (p.vec_store) goes through the warp's staging
+// tile [token][column] and leaves as 16-byte stores, 64 contiguous bytes per
+// token; ragged edges and the transposed layout are stored element by element.
+template <bool XBF16, int T>
+KL_DEVICE void pf_emit(const PfParams& p, uint8_t* stage, int col0, int ncols, int m0, int lane, const float (&o)[T]) {
+  if (p.vec_store && col0 + 32 <= ncols && m0 + T <= p.m) {
+    __syncwarp();                                    // previous step's reads of the tile are done
+#pragma unroll
+    for (int j = 0; j < T; ++j) store_act<XBF16>(stage, j * 32 + lane, o[j]);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < T * 64 / 16 / 32; ++it) {
+      const int v = it * 32 + lane, t = v >> 2, part = v & 3;
+      const uint4 val = *reinterpret_cast<const uint4*>(stage + t * 64 + part * 16);
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.y) +
+                                ((static_cast<long long>(m0 + t) * p.ldy + col0 + part * 8) << 1)) = val;
+    }
+    return;
+  }
+  const int col = col0 + lane;
+  if (col >= ncols) return;
+#pragma unroll
+  for (int j = 0; j < T; ++j) {
+    const int m = m0 + j;
+    if (m < p.m)
+      store_act<XBF16>(p.y, p.y_transposed ? static_cast<long long>(col) * p.ldy + m
+                                           : static_cast<long long>(m) * p.ldy + col, o[j]);
+  }
 }
 
 template <bool SWIGLU, bool XBF16>
@@ -247,6 +283,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
     const int q = warp & 3;
     const int r = q * 32 + lane;               // weight row of this CTA's 128
     const uint32_t lead_d_empty0 = mapa_shared(d_empty(0), 0);
+    uint8_t* stg = smem + L.stage + (warp - kPfEpi0) * kPfStageBytes;
     PfPipe pd{0, 2, 0};
     for (int it = 0; it < my_tiles; ++it) {
       const int t = pair + it * pairs;
@@ -258,59 +295,54 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
                    : "=r"(all_got) : "r"(got ? 1u : 0u) : "memory");
       if (!all_got) break;
       tc_fence_after();
-      // output column of this thread's row (gate rows for SwiGLU)
-      int col, wrow;
-      if constexpr (SWIGLU) {
-        col = nt * 128 + static_cast<int>(rank) * 64 + (r & 63);
-        wrow = r < 64 ? col : p.n_out + col;
-      } else {
-        col = nt * 256 + static_cast<int>(rank) * 128 + r;
-        wrow = col;
-      }
-      const bool row_ok = SWIGLU ? col < p.n_out : col < p.n;
-      const float s = row_ok ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[wrow]) : 0.0f;
+      // this warp's 32 output columns (gate rows for SwiGLU) and this thread's row
+      const int col0 = SWIGLU ? nt * 128 + static_cast<int>(rank) * 64 + (q & 1) * 32
+                              : nt * 256 + static_cast<int>(rank) * 128 + q * 32;
+      const int ncols = SWIGLU ? p.n_out : p.n;
+      const int col = col0 + lane;
+      const int wrow = SWIGLU ? (r < 64 ? col : p.n_out + col) : col;
+      const float s = col < ncols ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[wrow]) : 0.0f;
       const int m0 = mt * kPfTokens;
       const uint32_t d_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + kPfDCol0 + pd.idx * kPfTokens;
 #pragma unroll 1
-      for (int c = 0; c < kPfTokens / 16; ++c) {
-        uint32_t raw[16];
-        tmem_ld16(d_tmem + 16u * c, raw);
+      for (int c = 0; c < kPfTokens / kPfChunk; ++c) {
+        uint32_t lo[16], hi[16];
+        tmem_ld16(d_tmem + kPfChunk * c, lo);
+        tmem_ld16(d_tmem + kPfChunk * c + 16u, hi);
         tc_wait_ld();
-        if (c == kPfTokens / 16 - 1) {
+        if (c == kPfTokens / kPfChunk - 1) {
           // accumulator buffer fully read: release it to the leader's MMA
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(lead_d_empty0 + 8u * pd.idx);
         }
-        float v[16];
+        float v[kPfChunk];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(raw[j]) * s;
+        for (int j = 0; j < 16; ++j) {
+          v[j] = __uint_as_float(lo[j]) * s;
+          v[16 + j] = __uint_as_float(hi[j]) * s;
+        }
         if constexpr (SWIGLU) {
-          asm volatile("bar.sync 1, 128;" ::: "memory");        // previous chunk's reads done
-          if (r >= 64) {
+          // gate rows (r < 64) finish tokens 0..15 of the step, up rows (r >= 64)
+          // tokens 16..31; each hands the other half to its partner row r ^ 64
+          constexpr int H = kPfChunk / 2;
+          const bool gate = r < 64;
+          const int pr = r & 63;
+          asm volatile("bar.sync 1, 128;" ::: "memory");        // previous step's reads done
 #pragma unroll
-            for (int j = 0; j < 16; ++j) xch[(r - 64) * 16 + j] = v[j];
-          }
+          for (int j = 0; j < H; ++j) xch[(gate ? 0 : kPfXchHalf) + pr * (H + 1) + j] = gate ? v[H + j] : v[j];
           asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (r < 64 && row_ok) {
+          float o[H];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c * 16 + j;
-              if (m < p.m) {
-                const float o = swiglu_model_ordered<XBF16>(v[j], xch[r * 16 + j]);
-                store_act<XBF16>(p.y, p.y_transposed ? static_cast<long long>(col) * p.ldy + m
-                                                     : static_cast<long long>(m) * p.ldy + col, o);
-              }
-            }
+          for (int j = 0; j < H; ++j) {
+            const float other = xch[(gate ? kPfXchHalf : 0) + pr * (H + 1) + j];
+            const float g_val = gate ? v[j] : other;
+            const float u_val = gate ? other : v[H + j];
+            o[j] = swiglu_model_ordered_fast<XBF16>(g_val, u_val);
           }
-        } else if (row_ok) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c * 16 + j;
-            if (m < p.m)
-              store_act<XBF16>(p.y, p.y_transposed ? static_cast<long long>(col) * p.ldy + m
-                                                   : static_cast<long long>(m) * p.ldy + col, v[j]);
-          }
+          pf_emit<XBF16, H>(p, stg, col0, ncols, m0 + c * kPfChunk + (gate ? 0 : H), lane, o);
+        } else {
+          pf_emit<XBF16, kPfChunk>(p, stg, col0, ncols, m0 + c * kPfChunk, lane, v);
         }
       }
       pd.next();
