@@ -275,6 +275,27 @@ KL_DEVICE void s8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
   lo = fma_bf16x2(b0, 0xBF80BF80u, a0);                 // a - b
   hi = fma_bf16x2(b1, 0xBF80BF80u, a1);
 }
+// Exact int8 -> bf16 with half of the integer-pipe work moved to the FMA pipe.
+// With u = q ^ 0x80 = q + 128, the halfword 0x43uu is the bf16 value v = 128 + u
+// when u < 128 (q < 0) and v = 2u when u >= 128 (q >= 0: bit 7 of u lands in the
+// exponent), so r = v - 256 is q for q < 0 and 2q for q >= 0, and
+// q = r - relu(r) / 2.  Every intermediate is an integer with at most 8
+// significant bits, so each bf16 operation is exact.
+KL_DEVICE uint32_t fma_relu_bf16x2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.relu.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+KL_DEVICE void s8x4_to_bf16x4_fma(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t v0 = prmt(u, 0x43434343u, 0x4140u);    // [u0, 43, u1, 43]
+  const uint32_t v1 = prmt(u, 0x43434343u, 0x4342u);    // [u2, 43, u3, 43]
+  constexpr uint32_t kOne = 0x3F803F80u, kM256 = 0xC380C380u, kMHalf = 0xBF00BF00u;   // 1, -256, -0.5
+  const uint32_t r0 = fma_bf16x2(v0, kOne, kM256), r1 = fma_bf16x2(v1, kOne, kM256);
+  const uint32_t p0 = fma_relu_bf16x2(v0, kOne, kM256), p1 = fma_relu_bf16x2(v1, kOne, kM256);
+  lo = fma_bf16x2(p0, kMHalf, r0);
+  hi = fma_bf16x2(p1, kMHalf, r1);
+}
 // Same for f16: 0x6400|u is 1024+u for u < 1024; u = q ^ 0x80 = q + 128.
 KL_DEVICE void s8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
   const uint32_t u = w ^ 0x80808080u;

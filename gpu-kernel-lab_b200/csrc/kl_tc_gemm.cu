@@ -483,7 +483,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
-            if constexpr (XBF16) s8x4_to_bf16x4(wd[t], out[cc * 8 + 2 * t], out[cc * 8 + 2 * t + 1]);
+            if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t], out[cc * 8 + 2 * t], out[cc * 8 + 2 * t + 1]);
             else s8x4_to_f16x4(wd[t], out[cc * 8 + 2 * t], out[cc * 8 + 2 * t + 1]);
           }
         }

@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t4 = 0; t4 < 4; ++t4) {
-            if constexpr (XBF16) s8x4_to_bf16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
+            if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
             else s8x4_to_f16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
           }
         }
