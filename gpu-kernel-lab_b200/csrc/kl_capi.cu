@@ -134,6 +134,7 @@ int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
   pr.y_transposed = transposed ? 1 : 0;
+  pr.vec_store = (!transposed && aligned16(y) && ldy % 8 == 0) ? 1 : 0;
   tc_problem_tiles(pr, n_mma, kblk, swiglu != 0);
   return KL_OK;
 }

@@ -53,6 +53,7 @@ struct alignas(64) TcProblem {
   int m, n, k, n_out;                 // n = weight rows, n_out = output columns
   int m_tiles, n_tiles, kb_total;     // kb_total = k blocks per tile
   int y_transposed;
+  int vec_store;                      // row-major y, 16-byte aligned, ldy % 8 == 0: 16-byte stores
 };
 
 struct TcParams {

@@ -246,6 +246,25 @@ struct Epi {
                                int g) {
     const int m0 = mt * NMMA + cb * 16;
     if constexpr (!SWIGLU) {
+      // a warp's 32 rows x 16 tokens in range of a row-major output: stage them
+      // [token][row] in this warp's 1 KB of the (otherwise idle) exchange area
+      // and store 64 contiguous bytes per token as 16-byte vectors
+      const int n0 = nt * 128 + (r & ~31), lane = r & 31;
+      if (pr.vec_store && n0 + 32 <= pr.n_out && m0 + 16 <= pr.m) {
+        uint8_t* st = reinterpret_cast<uint8_t*>(xch + (r >> 5) * 256);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) store_act<XBF16>(st, j * 32 + lane, v[j]);
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const int vi = it * 32 + lane, t = vi >> 2, part = vi & 3;
+          const uint4 val = *reinterpret_cast<const uint4*>(st + t * 64 + part * 16);
+          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(pr.y) +
+                                    ((static_cast<long long>(m0 + t) * pr.ldy + n0 + part * 8) << 1)) = val;
+        }
+        return;
+      }
       const int n = nt * 128 + r;
       if (n < pr.n_out) {
 #pragma unroll
@@ -552,17 +571,27 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // 16 columns of the accumulator: the sum of the NI issuers' partial D regions
     auto load_d16 = [&](uint32_t d0, int cb, float (&v)[16]) {
-      uint32_t t[16];
-      tmem_ld16(d0 + 16u * cb, t);
-      tc_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(t[j]);
-#pragma unroll
-      for (int w = 1; w < Cfg::NI; ++w) {
-        tmem_ld16(d0 + static_cast<uint32_t>(w * Cfg::D_PITCH) + 16u * cb, t);
+      if constexpr (Cfg::NI == 2) {
+        // both issuers' partial regions in flight before one wait
+        uint32_t t0[16], t1[16];
+        tmem_ld16(d0 + 16u * cb, t0);
+        tmem_ld16(d0 + static_cast<uint32_t>(Cfg::D_PITCH) + 16u * cb, t1);
         tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(t[j]);
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(t0[j]) + __uint_as_float(t1[j]);
+      } else {
+        uint32_t t[16];
+        tmem_ld16(d0 + 16u * cb, t);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(t[j]);
+#pragma unroll
+        for (int w = 1; w < Cfg::NI; ++w) {
+          tmem_ld16(d0 + static_cast<uint32_t>(w * Cfg::D_PITCH) + 16u * cb, t);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(t[j]);
+        }
       }
     };
     Cursor ce;
