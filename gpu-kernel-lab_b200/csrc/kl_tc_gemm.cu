@@ -486,7 +486,29 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     Pipe pwc{0, SW, 0}, pa{0, A, 0};
     Cursor cc_;
     cc_.init(probs, u_lo, u_hi);
+    // 4-bit zero point of this thread's row for a unit (a global load, issued
+    // one unit ahead so its latency overlaps the previous unit's conversion)
+    auto load_zero = [&](const Cursor& cu) -> float {
+      if constexpr (FMT == KL_W4_ASYM) {
+        const TcProblem& pz = *cu.pr;
+        int zr = E::phys_row(pz, cu.nt, r);
+        zr = zr < pz.n ? zr : pz.n - 1;
+        return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pz.zeros)[static_cast<long long>(zr) * cu.kb_total + cu.kb]);
+      } else {
+        return 8.0f;
+      }
+    };
+    float z_cur = 8.0f;
+    if constexpr (is_w4<FMT>()) { if (n_local > 0) z_cur = load_zero(cc_); }
     for (int i = 0; i < n_local; ++i, cc_.next()) {
+      float z_next = 8.0f;
+      if constexpr (is_w4<FMT>()) {
+        if (i + 1 < n_local) {
+          Cursor nx = cc_;
+          nx.next();
+          z_next = load_zero(nx);
+        }
+      }
       if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
@@ -508,12 +530,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         }
       } else {
         // EPT nibbles = EPT/32 chunks of 16 B; 64B swizzle: chunk g at g ^ ((r >> 1) & 3)
-        const TcProblem& pr = *cc_.pr;
-        int prow = E::phys_row(pr, cc_.nt, r);
-        prow = prow < pr.n ? prow : pr.n - 1;
-        float z = 8.0f;
-        if constexpr (FMT == KL_W4_ASYM)
-          z = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.zeros)[static_cast<long long>(prow) * cc_.kb_total + cc_.kb]);
+        const float z = z_cur;
         const uint32_t bias = XBF16 ? pack_bf16x2(-(128.0f + z), -(128.0f + z))
                                     : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
@@ -552,6 +569,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       }
       pwc.next();
       pa.next();
+      z_cur = z_next;
     }
   } else {
     // ---------------------------------------------------------------- epilogue
@@ -613,10 +631,18 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       if (!chunk_end) continue;
       const int my_chunk = chunk++;
       if (Roles::EPI_GROUPS == 2 && (my_chunk & 1) != eg) continue;
+      const int prow = E::phys_row(pr, nt, r);
+      float gs = 1.0f;                         // group scale, loaded before the wait
+      if constexpr (grouped<FMT>()) {
+        const int pr_row = prow < pr.n ? prow : pr.n - 1;
+        if constexpr (FMT == KL_W4_ASYM)
+          gs = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb]);
+        else
+          gs = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb];
+      }
       if (!(ok = wait_bar(d_full(pd.idx), pd.phase, abort_flag, p.status))) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + lane_base + Cfg::d_col(pd.idx, 0);
-      const int prow = E::phys_row(pr, nt, r);
       const bool full_tile = seg_end && seg_kb0 == 0 && ce.kb == ce.kb_total - 1;
       float* part_base = nullptr;
       if (seg_end && !full_tile) {
@@ -624,12 +650,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
       }
       if constexpr (grouped<FMT>()) {
-        const int pr_row = prow < pr.n ? prow : pr.n - 1;
-        float s;
-        if constexpr (FMT == KL_W4_ASYM)
-          s = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb]);
-        else
-          s = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb];
+        const float s = gs;
 #pragma unroll
         for (int cb = 0; cb < NMMA / 16; ++cb) {
           float v[16];
