@@ -117,8 +117,10 @@ int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const
                   int n_mma, int kblk) {
   std::memset(&pr, 0, sizeof(pr));
   int rc;
-  if (is_w4(w_format))
+  if (is_w4(w_format) && kblk == 128)
     rc = encode_2d(&pr.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k / 2, n, k / 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+  else if (is_w4(w_format))
+    rc = encode_2d(&pr.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k / 2, n, k / 2, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   else
     rc = encode_2d(&pr.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != KL_OK) return rc;
@@ -152,6 +154,7 @@ long long problem_units(int m, int n, int k, int n_mma, int kblk, bool swiglu) {
 
 // K block for one GEMM on this device.
 int choose_kblk_single(int m, int n, int k, int fmt, int n_mma, bool swiglu, int sm_count) {
+  if (is_w4(fmt) && k % 256) return 128;
   return tc_choose_kblk(fmt, n_mma, problem_units(m, n, k, n_mma, 256, swiglu), sm_count);
 }
 
@@ -374,6 +377,10 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
   for (int i = 0; i < count; ++i)
     units256 += problem_units(problems[i].m, problems[i].n, problems[i].k, hd->n_mma, 256, swiglu != 0);
   hd->kblk = tc_choose_kblk(w_format, hd->n_mma, units256, sm);
+  if (hd->kblk == 256 && is_w4(w_format)) {   // two 128-groups per stage need K % 256 == 0 everywhere
+    for (int i = 0; i < count; ++i)
+      if (problems[i].k % 256) hd->kblk = 128;
+  }
   long long units = 0;
   for (int i = 0; i < count; ++i) {
     const kl_problem& q = problems[i];

@@ -309,10 +309,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   using Cfg = TcCfg<NMMA, KBL>;
   using Roles = TcRoles<FMT, NMMA, KBL>;
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
-  static_assert(!grouped<FMT>() || KBL == 128, "4-bit group mode: one group of 128 per stage");
+  static_assert(!grouped<FMT>() || KBL == 128 || (KBL == 256 && NMMA == 16), "4-bit group mode: one or two groups of 128 per stage");
   constexpr int WSB = w_stage_bytes<FMT, KBL>();
   constexpr int ROW_BYTES = w_row_bytes<FMT, KBL>();      // bytes of one tile row per stage
-  constexpr int SPAN = is_w4<FMT>() ? 64 : 128;           // swizzle span = TMA box inner bytes
+  constexpr int SPAN = (is_w4<FMT>() && KBL == 128) ? 64 : 128;   // swizzle span = TMA box inner bytes
   constexpr int NBLK = ROW_BYTES / SPAN;                  // column blocks per stage
   constexpr int BLK = 128 * SPAN;                         // bytes of one column block
   constexpr int A = Cfg::A_STAGES;
@@ -493,7 +493,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         const TcProblem& pz = *cu.pr;
         int zr = E::phys_row(pz, cu.nt, r);
         zr = zr < pz.n ? zr : pz.n - 1;
-        return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pz.zeros)[static_cast<long long>(zr) * cu.kb_total + cu.kb]);
+        // groups of 128 along K; this thread's slice of the stage lies in one group
+        constexpr int GPS = KBL / 128;
+        const int grp = cu.kb * GPS + (h * Roles::EPT) / 128;
+        return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pz.zeros)[static_cast<long long>(zr) * cu.kb_total * GPS + grp]);
       } else {
         return 8.0f;
       }
@@ -513,7 +516,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
       const uint8_t* wstage = smem + L.w + pwc.idx * WSB;
-      uint32_t out[EPT / 2];
+      uint32_t out[is_w4<FMT>() ? 1 : EPT / 2];
       if constexpr (!is_w4<FMT>()) {
         // EPT int8 = EPT/16 chunks of 16 B; chunk g of the stage row sits in column
         // block g/8 at position (g%8) ^ (r & 7) (128B swizzle)
@@ -535,30 +538,39 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
                                     : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
                                          : (FMT == KL_W4_SYM ? 0x64086408u : 0x64006400u);
+        // each 16-byte chunk (32 nibbles) is 16 TMEM columns: convert and store it at once
+        const uint32_t a_tmem4 = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(Cfg::ACOLS) * pa.idx + static_cast<uint32_t>(EPT / 2) * h;
 #pragma unroll
         for (int cc = 0; cc < EPT / 32; ++cc) {
           const int g = h * (EPT / 32) + cc;
-          const uint4 v = *reinterpret_cast<const uint4*>(wstage + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+          uint32_t part[16];
+          // 64-byte rows (64B swizzle) for 128-wide stages, 128-byte rows (128B swizzle) for 256
+          const uint4 v = KBL == 128 ? *reinterpret_cast<const uint4*>(wstage + r * 64 + ((g ^ ((r >> 1) & 3)) << 4))
+                                     : *reinterpret_cast<const uint4*>(wstage + r * 128 + ((g ^ (r & 7)) << 4));
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const uint32_t sh = wd[t] >> 4;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-              out[cc * 16 + t * 4 + b] = XBF16 ? u4x2_to_bf16x2(wd[t], sh, nib_sel(b), magic, bias)
-                                               : u4x2_to_f16x2(wd[t], sh, nib_sel(b), magic, bias);
+              part[t * 4 + b] = XBF16 ? u4x2_to_bf16x2(wd[t], sh, nib_sel(b), magic, bias)
+                                      : u4x2_to_f16x2(wd[t], sh, nib_sel(b), magic, bias);
             }
           }
+          tmem_st16(a_tmem4 + 16u * cc, part);
         }
       }
-      const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
-                              static_cast<uint32_t>(EPT / 2) * h;
+      if constexpr (!is_w4<FMT>()) {
+        const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
+                                static_cast<uint32_t>(EPT / 2) * h;
 #pragma unroll
-      for (int j = 0; j < EPT / 32; ++j) {
-        uint32_t part[16];
+        for (int j = 0; j < EPT / 32; ++j) {
+          uint32_t part[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) part[t] = out[16 * j + t];
-        tmem_st16(a_tmem + 16u * j, part);
+          for (int t = 0; t < 16; ++t) part[t] = out[16 * j + t];
+          tmem_st16(a_tmem + 16u * j, part);
+        }
       }
       tc_wait_st();
       tc_fence_before();
@@ -632,13 +644,20 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       const int my_chunk = chunk++;
       if (Roles::EPI_GROUPS == 2 && (my_chunk & 1) != eg) continue;
       const int prow = E::phys_row(pr, nt, r);
-      float gs = 1.0f;                         // group scale, loaded before the wait
+      constexpr int GPS = grouped<FMT>() ? KBL / 128 : 1;    // 128-groups per stage
+      float gs[GPS];                           // group scales, loaded before the wait
+#pragma unroll
+      for (int gi = 0; gi < GPS; ++gi) gs[gi] = 1.0f;
       if constexpr (grouped<FMT>()) {
         const int pr_row = prow < pr.n ? prow : pr.n - 1;
-        if constexpr (FMT == KL_W4_ASYM)
-          gs = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb]);
-        else
-          gs = reinterpret_cast<const float*>(pr.scales)[static_cast<long long>(pr_row) * ce.kb_total + ce.kb];
+        const long long sbase = static_cast<long long>(pr_row) * ce.kb_total * GPS + ce.kb * GPS;
+#pragma unroll
+        for (int gi = 0; gi < GPS; ++gi) {
+          if constexpr (FMT == KL_W4_ASYM)
+            gs[gi] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[sbase + gi]);
+          else
+            gs[gi] = reinterpret_cast<const float*>(pr.scales)[sbase + gi];
+        }
       }
       if (!(ok = wait_bar(d_full(pd.idx), pd.phase, abort_flag, p.status))) break;
       tc_fence_after();
@@ -650,13 +669,31 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
       }
       if constexpr (grouped<FMT>()) {
-        const float s = gs;
+        if constexpr (GPS == 1) {
+          const float s = gs[0];
 #pragma unroll
-        for (int cb = 0; cb < NMMA / 16; ++cb) {
-          float v[16];
-          load_d16(d_tmem, cb, v);
+          for (int cb = 0; cb < NMMA / 16; ++cb) {
+            float v[16];
+            load_d16(d_tmem, cb, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, v[j], acc[cb * 16 + j]);
+            for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, v[j], acc[cb * 16 + j]);
+          }
+        } else {
+          // two groups per stage: issuers [0, NI/2) hold group 0, [NI/2, NI) group 1
+          static_assert(GPS == 2 && Cfg::NI == 4, "two-group stages use four issuers");
+#pragma unroll
+          for (int cb = 0; cb < NMMA / 16; ++cb) {
+#pragma unroll
+            for (int gi = 0; gi < 2; ++gi) {
+              uint32_t t0[16], t1[16];
+              tmem_ld16(d_tmem + static_cast<uint32_t>((2 * gi) * Cfg::D_PITCH) + 16u * cb, t0);
+              tmem_ld16(d_tmem + static_cast<uint32_t>((2 * gi + 1) * Cfg::D_PITCH) + 16u * cb, t1);
+              tc_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                acc[cb * 16 + j] = fmaf(gs[gi], __uint_as_float(t0[j]) + __uint_as_float(t1[j]), acc[cb * 16 + j]);
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -811,6 +848,9 @@ cudaError_t launch_nmma(const TcParams& p, const TcPlan& plan, bool pdl, cudaStr
         default: return cudaErrorInvalidValue;
       }
     }
+  } else if constexpr (grouped<FMT>()) {
+    if (plan.kblk == 256)   // two 128-groups per stage: 16-token tiles only
+      return plan.n_mma == 16 ? launch_one<FMT, 16, 256, SWIGLU, XBF16>(p, plan, pdl, s) : cudaErrorInvalidValue;
   }
   if (plan.kblk != 128) return cudaErrorInvalidValue;
   switch (plan.n_mma) {
@@ -858,6 +898,8 @@ static int tc_a_stages(int n_mma, int kblk) {
 }
 
 int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count) {
+  if (fmt == KL_W4_SYM || fmt == KL_W4_ASYM)   // callers also require K % 256 == 0
+    return (n_mma == 16 && units_at_256 >= 2ll * sm_count) ? 256 : 128;
   if (fmt != KL_W8_ROW || n_mma > 64) return 128;
   return units_at_256 >= 2ll * sm_count ? 256 : 128;
 }
@@ -880,7 +922,7 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   t.ok = false;
   if (units <= 0 || sm_count <= 0) return t;
   const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
-  if (!(kblk == 128 || (kblk == 256 && fmt == KL_W8_ROW && n_mma <= 64))) return t;
+  if (!(kblk == 128 || (kblk == 256 && fmt == KL_W8_ROW && n_mma <= 64) || (kblk == 256 && w4 && n_mma == 16))) return t;
   t.n_mma = n_mma;
   t.kblk = kblk;
   t.units = units;
