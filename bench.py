@@ -401,13 +401,21 @@ def bench_decode(args, kl, world, rank, local, dist):
             for _ in range(3):
                 shead(x, gathered=gathered)
             barrier()
+            # shard GEMM + all-gather captured once and replayed (no host launch gaps);
+            # the graph is released before the process group is torn down
+            sg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(sg):
+                shead(x, gathered=gathered)
+            sg.replay()
+            barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             reps = max(5, args.steps)
             a.record()
             for _ in range(reps):
-                shead(x, gathered=gathered)
+                sg.replay()
             b.record()
             barrier()
+            del sg
             t = a.elapsed_time(b) / reps
             if dist is not None:
                 tt = torch.tensor([t], device=device)

@@ -136,7 +136,7 @@ int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
   pr.y_transposed = transposed ? 1 : 0;
-  pr.vec_store = (!transposed && aligned16(y) && ldy % 8 == 0) ? 1 : 0;
+  pr.vec_store = (aligned16(y) && ldy % 8 == 0) ? (transposed ? 2 : 1) : 0;
   tc_problem_tiles(pr, n_mma, kblk, swiglu != 0);
   return KL_OK;
 }
@@ -261,7 +261,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     p.k = k;
     p.n_out = n_out;
     p.y_transposed = transposed ? 1 : 0;
-    p.vec_store = (!transposed && aligned16(y) && p.ldy % 8 == 0) ? 1 : 0;
+    p.vec_store = (aligned16(y) && p.ldy % 8 == 0) ? (transposed ? 2 : 1) : 0;
     p.status = di.status;
     prefill_tiles(p, swiglu != 0);
     const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, s);

@@ -53,7 +53,7 @@ struct alignas(64) TcProblem {
   int m, n, k, n_out;                 // n = weight rows, n_out = output columns
   int m_tiles, n_tiles, kb_total;     // kb_total = k blocks per tile
   int y_transposed;
-  int vec_store;                      // row-major y, 16-byte aligned, ldy % 8 == 0: 16-byte stores
+  int vec_store;                      // y 16-byte aligned, ldy % 8 == 0: 16-byte stores (1 row-major, 2 transposed)
 };
 
 struct TcParams {
@@ -95,7 +95,7 @@ struct PfParams {
   int m, n, k, n_out;
   int n_tiles, m_tiles, kb_total;
   int y_transposed;
-  int vec_store;                      // row-major y, 16-byte aligned, ldy % 8 == 0: 16-byte stores
+  int vec_store;                      // y 16-byte aligned, ldy % 8 == 0: 16-byte stores (1 row-major, 2 transposed)
   int* status;
 };
 int prefill_threads();

@@ -250,7 +250,7 @@ struct Epi {
       // [token][row] in this warp's 1 KB of the (otherwise idle) exchange area
       // and store 64 contiguous bytes per token as 16-byte vectors
       const int n0 = nt * 128 + (r & ~31), lane = r & 31;
-      if (pr.vec_store && n0 + 32 <= pr.n_out && m0 + 16 <= pr.m) {
+      if (pr.vec_store == 1 && n0 + 32 <= pr.n_out && m0 + 16 <= pr.m) {
         uint8_t* st = reinterpret_cast<uint8_t*>(xch + (r >> 5) * 256);
         __syncwarp();
 #pragma unroll
@@ -266,6 +266,16 @@ struct Epi {
         return;
       }
       const int n = nt * 128 + r;
+      if (pr.vec_store == 2 && n < pr.n_out && m0 + 16 <= pr.m) {
+        // transposed output: this row's 16 tokens are contiguous, two 16-byte stores
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pk[j] = XBF16 ? pack_bf16x2(v[2 * j], v[2 * j + 1]) : pack_f16x2(v[2 * j], v[2 * j + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(pr.y) + ((static_cast<long long>(n) * pr.ldy + m0) << 1));
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        return;
+      }
       if (n < pr.n_out) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {

@@ -97,7 +97,21 @@ KL_DEVICE bool pf_wait_warp(uint32_t bar, uint32_t parity, int* status) {
 // token; ragged edges and the transposed layout are stored element by element.
 template <bool XBF16, int T>
 KL_DEVICE void pf_emit(const PfParams& p, uint8_t* stage, int col0, int ncols, int m0, int lane, const float (&o)[T]) {
-  if (p.vec_store && col0 + 32 <= ncols && m0 + T <= p.m) {
+  if (p.vec_store == 2 && col0 + lane < ncols && m0 + T <= p.m) {
+    // transposed output: this column's T tokens are contiguous, 16-byte stores
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.y) +
+                                          ((static_cast<long long>(col0 + lane) * p.ldy + m0) << 1));
+#pragma unroll
+    for (int v4 = 0; v4 < T / 8; ++v4) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        pk[j] = XBF16 ? pack_bf16x2(o[8 * v4 + 2 * j], o[8 * v4 + 2 * j + 1]) : pack_f16x2(o[8 * v4 + 2 * j], o[8 * v4 + 2 * j + 1]);
+      dst[v4] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    return;
+  }
+  if (p.vec_store == 1 && col0 + 32 <= ncols && m0 + T <= p.m) {
     __syncwarp();                                    // previous step's reads of the tile are done
 #pragma unroll
     for (int j = 0; j < T; ++j) store_act<XBF16>(stage, j * 32 + lane, o[j]);
