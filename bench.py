@@ -421,8 +421,29 @@ def bench_decode(args, kl, world, rank, local, dist):
                 tt = torch.tensor([t], device=device)
                 dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                 t = tt.item()
+            # fused alternative: shard GEMM + local top-8 + gather of candidates + merge
+            for _ in range(3):
+                shead.topk(x, 8)
+            barrier()
+            tg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(tg):
+                shead.topk(x, 8)
+            tg.replay()
+            barrier()
+            a.record()
+            for _ in range(reps):
+                tg.replay()
+            b.record()
+            barrier()
+            del tg
+            tk = a.elapsed_time(b) / reps
+            if dist is not None:
+                tt = torch.tensor([tk], device=device)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                tk = tt.item()
             sharded["per_m"][str(m)] = {"ms": round(t, 4), "allgather_bytes": vocab * m * 2,
-                                        "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1)}
+                                        "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1),
+                                        "top8_ms": round(tk, 4), "top8_gather_bytes": world * m * 8 * 8}
 
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     result = {

@@ -496,6 +496,35 @@ int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w, co
   return KL_OK;
 }
 
+size_t kl_topk_rows_workspace_bytes(int rows, int n, int top_k) {
+  if (rows <= 0 || n <= 0 || top_k <= 0) return 0;
+  return topk_rows_candidate_bytes(rows, n, top_k);
+}
+
+int kl_topk_rows(const void* logits, int dtype, int rows, int n, long long ld, long long index_offset, int top_k,
+                 float* values, int64_t* ids, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!logits || !ids) return fail(KL_ERR_INVALID, "logits and ids must be non-null");
+  if (dtype != KL_DT_BF16 && dtype != KL_DT_F16) return fail(KL_ERR_INVALID, "logits must be bf16 or f16");
+  if (rows <= 0 || n <= 0 || ld < n) return fail(KL_ERR_INVALID, "need rows > 0, n > 0 and ld >= n");
+  if (top_k < 1 || top_k > 8 || top_k > n) return fail(KL_ERR_INVALID, "top_k must be in [1, min(8, n)]");
+  if (index_offset < 0) return fail(KL_ERR_INVALID, "index_offset must be non-negative");
+  const size_t need = topk_rows_candidate_bytes(rows, n, top_k);
+  if (!workspace || workspace_bytes < need) return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+  const cudaError_t e = launch_topk_rows(logits, dtype == KL_DT_BF16, rows, n, ld, index_offset, top_k, workspace,
+                                         values, ids, static_cast<cudaStream_t>(stream), values == nullptr);
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "top-k launch");
+}
+
+int kl_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
+                       void* stream) {
+  if (!packed || !values || !ids) return fail(KL_ERR_INVALID, "pointers must be non-null");
+  if (rows <= 0 || count <= 0) return fail(KL_ERR_INVALID, "need rows > 0 and count > 0");
+  if (top_k < 1 || top_k > 8 || top_k > count) return fail(KL_ERR_INVALID, "top_k must be in [1, min(8, count)]");
+  const cudaError_t e = launch_topk_merge_rows(packed, rows, count, top_k, values, ids,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "top-k merge launch");
+}
+
 int kl_quantize_w8_row(const void* w, int w_dtype, int n, int k, int8_t* q, void* scale_bf16, void* stream) {
   if (!w || !q || !scale_bf16) return fail(KL_ERR_INVALID, "null pointer");
   if (n <= 0 || k <= 0) return fail(KL_ERR_INVALID, "weight must be a nonempty [N,K] matrix");

@@ -115,6 +115,16 @@ __host__ __device__ inline long long unit_owner(long long u, long long units, lo
   return ((u + 1) * grid + units - 1) / units - 1;
 }
 
+// ------------------------------------------------------------------ top-k
+// Per-row top-k over logits rows (value descending, lower index first on ties).
+size_t head_topk_candidate_bytes(int n, int top_k);
+size_t topk_rows_candidate_bytes(int rows, int n, int top_k);
+// packed_out: ids receives (id << 32 | f32 value bits) pairs and values is unused
+cudaError_t launch_topk_rows(const void* logits, bool xbf16, int rows, int n, long long ld, long long index_offset,
+                             int top_k, void* cand, float* values, int64_t* ids, cudaStream_t s, bool packed_out);
+cudaError_t launch_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
+                                   cudaStream_t s);
+
 // ---------------------------------------------------------- quantisation
 cudaError_t launch_quantize_w8_row(const void* w, int w_dtype, int n, int k, int8_t* q, void* scale, cudaStream_t s);
 cudaError_t launch_quantize_w4(const void* w, int w_dtype, int n, int k, int group, int fmt,

@@ -179,22 +179,29 @@ KL_DEVICE void block_best(float& v, long long& idx, float* sv, long long* si) {
     if (better(sv[i], si[i], v, idx)) { v = sv[i]; idx = si[i]; }
 }
 
-// Stage 1: logits (activation dtype) -> per-block top-k candidates.
+// Stage 1: logits (activation dtype) -> per-block top-k candidates, one row of
+// logits per blockIdx.y (row stride `ld` elements); candidate ids are the
+// element index plus `index_offset` (a vocabulary shard's first row).
 template <bool XBF16>
-__global__ void __launch_bounds__(kTopkThreads) topk_candidates_kernel(const void* logits, int n, int top_k,
+__global__ void __launch_bounds__(kTopkThreads) topk_candidates_kernel(const void* logits, int n, long long ld,
+                                                                       long long index_offset, int top_k,
                                                                        float* cand_v, long long* cand_i) {
   __shared__ float sv[32];
   __shared__ long long si[32];
   float v[kTopkPerThread];
   long long id[kTopkPerThread];
+  const long long row = blockIdx.y;
   const long long base = static_cast<long long>(blockIdx.x) * kTopkBlockItems;
+  const long long row0 = row * ld;
 #pragma unroll
   for (int j = 0; j < kTopkPerThread; ++j) {
     const long long i = base + j * kTopkThreads + threadIdx.x;
-    id[j] = i;
-    v[j] = i < n ? load_act<XBF16>(logits, i) : -INFINITY;
+    id[j] = i + index_offset;
+    v[j] = i < n ? load_act<XBF16>(logits, row0 + i) : -INFINITY;
     if (i >= n) id[j] = 0x7fffffffffffffffll;
   }
+  cand_v += (row * gridDim.x) * top_k;
+  cand_i += (row * gridDim.x) * top_k;
   for (int r = 0; r < top_k; ++r) {
     float bv = -INFINITY;
     long long bi = 0x7fffffffffffffffll;
@@ -212,25 +219,48 @@ __global__ void __launch_bounds__(kTopkThreads) topk_candidates_kernel(const voi
   }
 }
 
-// Stage 2: one block merges all candidates.
+// A (value, id) candidate packed in 64 bits: id in the high word, the f32
+// value's bits in the low word (ids < 2^31).
+KL_DEVICE long long pack_cand(float v, long long id) {
+  return static_cast<long long>(static_cast<unsigned long long>(id) << 32 |
+                                static_cast<unsigned long long>(__float_as_uint(v)));
+}
+KL_DEVICE float cand_value(long long p) { return __uint_as_float(static_cast<unsigned>(p & 0xFFFFFFFFll)); }
+KL_DEVICE long long cand_id(long long p) { return static_cast<long long>(static_cast<unsigned long long>(p) >> 32); }
+
+// Stage 2: one block per row merges that row's `count` candidates, given as
+// separate arrays or packed (PACKED_IN), and writes the row's top-k as values +
+// ids, or packed (PACKED_OUT, for an all-gather across ranks).
+template <bool PACKED_IN, bool PACKED_OUT>
 __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(const float* cand_v, const long long* cand_i,
                                                                   int count, int top_k, float* values, int64_t* ids) {
   __shared__ float sv[32];
   __shared__ long long si[32];
   __shared__ long long chosen[8];
+  const long long row = blockIdx.x;
+  if constexpr (!PACKED_IN) cand_v += row * count;
+  cand_i += row * count;
+  if constexpr (!PACKED_OUT) values += row * top_k;
+  ids += row * top_k;
   for (int r = 0; r < top_k; ++r) {
     float bv = -INFINITY;
     long long bi = 0x7fffffffffffffffll;
     for (int i = threadIdx.x; i < count; i += blockDim.x) {
+      const float cv = PACKED_IN ? cand_value(cand_i[i]) : cand_v[i];
+      const long long ci = PACKED_IN ? cand_id(cand_i[i]) : cand_i[i];
       bool taken = false;
-      for (int q = 0; q < r; ++q) taken |= (cand_i[i] == chosen[q]);
-      if (!taken && better(cand_v[i], cand_i[i], bv, bi)) { bv = cand_v[i]; bi = cand_i[i]; }
+      for (int q = 0; q < r; ++q) taken |= (ci == chosen[q]);
+      if (!taken && better(cv, ci, bv, bi)) { bv = cv; bi = ci; }
     }
     block_best(bv, bi, sv, si);
     if (threadIdx.x == 0) {
       chosen[r] = bi;
-      values[r] = bv;
-      ids[r] = bi;
+      if constexpr (PACKED_OUT) {
+        ids[r] = pack_cand(bv, bi);
+      } else {
+        values[r] = bv;
+        ids[r] = bi;
+      }
     }
     __syncthreads();
   }
@@ -265,15 +295,33 @@ size_t head_topk_candidate_bytes(int n, int top_k) {
 
 cudaError_t launch_topk(const void* logits, bool xbf16, int n, int top_k, void* cand, float* values,
                         int64_t* ids, cudaStream_t s) {
+  return launch_topk_rows(logits, xbf16, 1, n, n, 0, top_k, cand, values, ids, s, false);
+}
+
+size_t topk_rows_candidate_bytes(int rows, int n, int top_k) {
+  return static_cast<size_t>(rows) * (head_topk_candidate_bytes(n, top_k) - 256) + 256;
+}
+
+cudaError_t launch_topk_rows(const void* logits, bool xbf16, int rows, int n, long long ld, long long index_offset,
+                             int top_k, void* cand, float* values, int64_t* ids, cudaStream_t s, bool packed_out) {
   const int blocks = (n + kTopkBlockItems - 1) / kTopkBlockItems;
   float* cv = reinterpret_cast<float*>(cand);
   long long* ci = reinterpret_cast<long long*>(
-      (reinterpret_cast<uintptr_t>(cv + static_cast<size_t>(blocks) * top_k) + 15) & ~uintptr_t(15));
-  if (xbf16) topk_candidates_kernel<true><<<blocks, kTopkThreads, 0, s>>>(logits, n, top_k, cv, ci);
-  else topk_candidates_kernel<false><<<blocks, kTopkThreads, 0, s>>>(logits, n, top_k, cv, ci);
+      (reinterpret_cast<uintptr_t>(cv + static_cast<size_t>(rows) * blocks * top_k) + 15) & ~uintptr_t(15));
+  const dim3 grid(blocks, rows);
+  if (xbf16) topk_candidates_kernel<true><<<grid, kTopkThreads, 0, s>>>(logits, n, ld, index_offset, top_k, cv, ci);
+  else topk_candidates_kernel<false><<<grid, kTopkThreads, 0, s>>>(logits, n, ld, index_offset, top_k, cv, ci);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  topk_merge_kernel<<<1, kTopkThreads, 0, s>>>(cv, ci, blocks * top_k, top_k, values, ids);
+  if (packed_out) topk_merge_kernel<false, true><<<rows, kTopkThreads, 0, s>>>(cv, ci, blocks * top_k, top_k, values, ids);
+  else topk_merge_kernel<false, false><<<rows, kTopkThreads, 0, s>>>(cv, ci, blocks * top_k, top_k, values, ids);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
+                                   cudaStream_t s) {
+  topk_merge_kernel<true, false><<<rows, kTopkThreads, 0, s>>>(nullptr, reinterpret_cast<const long long*>(packed),
+                                                               count, top_k, values, ids);
   return cudaGetLastError();
 }
 

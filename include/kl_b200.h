@@ -193,6 +193,27 @@ int kl_device_status(int device, int reset);
 int kl_version(void);
 
 /*
+ * Top-k over rows of logits, for lm_heads whose logits are split across GPUs:
+ * the candidate and merge stages of learning/09_int4/kernels.py:37-50 and
+ * :77-99 (tile-local top-k, then a merge; value descending, the lower index
+ * first on ties), generalised to `rows` rows and to an index offset.
+ *   kl_topk_rows: logits [rows, ld] (bf16/f16, first n of each row used) ->
+ *     values f32 [rows, top_k], ids int64 [rows, top_k] = column + index_offset
+ *     (a vocabulary shard passes its first row).  1 <= top_k <= 8.  With
+ *     values == NULL, ids receives packed candidates instead: (id << 32) | the
+ *     f32 value's bits, one int64 per candidate (ids < 2^31), ready to gather.
+ *   kl_topk_merge_rows: packed candidates int64 [rows, count] (every rank's
+ *     packed kl_topk_rows output, gathered) -> values f32 / ids int64
+ *     [rows, top_k], the rows' global top_k.
+ */
+size_t kl_topk_rows_workspace_bytes(int rows, int n, int top_k);
+int kl_topk_rows(const void* logits, int dtype, int rows, int n, long long ld,
+                 long long index_offset, int top_k, float* values, int64_t* ids,
+                 void* workspace, size_t workspace_bytes, void* stream);
+int kl_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k,
+                       float* values, int64_t* ids, void* stream);
+
+/*
  * Host-only description of the launch plan kl_linear would use on a device
  * with `sm_count` SMs, and a self-check of its work partition (every
  * (tile, k-block) unit covered exactly once, workspace slots in bounds).
