@@ -128,6 +128,7 @@ def act_dtype_code(dtype: torch.dtype) -> int:
 # Calls on different streams of one device that could overlap should pass their
 # own workspace (see ``linear.quant_linear(workspace=...)``).
 _workspaces: dict[int, torch.Tensor] = {}
+_retired_workspaces: list = []
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
@@ -140,6 +141,9 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
             raise RuntimeError("the first quantized-linear call on a device must happen before CUDA-graph "
                                "capture (it allocates the device workspace); run one warm-up call first")
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        if idx in _workspaces:
+            # CUDA graphs captured earlier may still point at the old buffer: keep it alive
+            _retired_workspaces.append(_workspaces[idx])
         _workspaces[idx] = buf
     return buf
 
