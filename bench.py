@@ -496,13 +496,15 @@ def bench_prefill(args, kl, world, rank, local, dist):
                 items.append((name, p, sw, x, y))
             for _ in range(args.warmup):
                 for name, p, sw, x, y in items:
-                    kl.quant_linear(x, p, out=y, swiglu=sw)
+                    kl.quant_linear(x, p, out=y, swiglu=sw, pdl=True)
             torch.cuda.synchronize()
-            # the layer's four GEMMs as one CUDA graph (no host launch gaps)
+            # the layer's four GEMMs as one CUDA graph (no host launch gaps); with
+            # programmatic dependent launch each GEMM's set-up and weight stream
+            # overlap the previous GEMM's tail
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 for name, p, sw, x, y in items:
-                    kl.quant_linear(x, p, out=y, swiglu=sw)
+                    kl.quant_linear(x, p, out=y, swiglu=sw, pdl=True)
             for _ in range(args.warmup):
                 graph.replay()
             torch.cuda.synchronize()
@@ -524,7 +526,7 @@ def bench_prefill(args, kl, world, rank, local, dist):
             "warmup": args.warmup, "ms_per_step": round(total_ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "qwen3-0.6b prefill layer GEMMs (BASELINE config 2)", "batch_m": ms_list,
-                       "swiglu": bool(args.swiglu), "launch": "the 4 layer GEMMs of each M as one CUDA graph",
+                       "swiglu": bool(args.swiglu), "launch": "the 4 layer GEMMs of each M as one CUDA graph, programmatic dependent launch",
                        "l2": "no flush: at M>=2048 each graph replay streams more than the 126 MB L2 in activations and outputs"},
             "per_m": res,
             "roofline": {"bound": "tensor", "achieved": round(value / world, 1), "peak": tf_burst, "unit": "TFLOP/s",

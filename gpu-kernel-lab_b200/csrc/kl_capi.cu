@@ -264,7 +264,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     p.vec_store = (aligned16(y) && p.ldy % 8 == 0) ? (transposed ? 2 : 1) : 0;
     p.status = di.status;
     prefill_tiles(p, swiglu != 0);
-    const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, s);
+    const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 pair GEMM launch");
     return KL_OK;
   }

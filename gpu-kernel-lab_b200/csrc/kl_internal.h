@@ -103,7 +103,7 @@ int prefill_smem_bytes();
 int prefill_k_block();
 void prefill_tiles(PfParams& p, bool swiglu);
 int prefill_grid(const PfParams& p, int sm_count);
-cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, cudaStream_t s);
+cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
 // Work partition shared by the kernel and the host-side self-check:
 // CTA c owns units [lo(c), lo(c+1)) with lo(c) = floor(c * units / grid).

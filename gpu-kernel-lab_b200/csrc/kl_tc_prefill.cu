@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   cluster_sync();                              // barrier inits and TMEM allocation visible to the pair
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ---------------------------------------------------------- weight TMA
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
     // ----------------------------------------------------------- token TMA
     if (lane == 0 && my_tiles > 0) {
       prefetch_tmap(&p.tmap_x);
+      pdl_wait();                              // tokens come from the previous kernel
       const uint32_t lead_full0 = mapa_shared(x_full(0), 0);
       PfPipe px{0, kPfX, 0};
       for (int it = 0; it < my_tiles; ++it) {
@@ -298,6 +300,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
     const int r = q * 32 + lane;               // weight row of this CTA's 128
     const uint32_t lead_d_empty0 = mapa_shared(d_empty(0), 0);
     uint8_t* stg = smem + L.stage + (warp - kPfEpi0) * kPfStageBytes;
+    pdl_wait();                                // y is written only after the previous kernel
     PfPipe pd{0, 2, 0};
     for (int it = 0; it < my_tiles; ++it) {
       const int t = pair + it * pairs;
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
 }
 
 template <bool SWIGLU, bool XBF16>
-cudaError_t launch_pf(const PfParams& p, int grid, cudaStream_t s) {
+cudaError_t launch_pf(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
   auto kern = tc_prefill_kernel<SWIGLU, XBF16>;
   constexpr int smem = static_cast<int>(pf_layout().total);
   static bool attr[kMaxDevices] = {};
@@ -390,11 +393,13 @@ cudaError_t launch_pf(const PfParams& p, int grid, cudaStream_t s) {
   cfg.blockDim = dim3(kPfThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   // no more pairs than can be resident at once (a GPC with an odd number of
@@ -411,6 +416,9 @@ cudaError_t launch_pf(const PfParams& p, int grid, cudaStream_t s) {
     }
     if (grid / 2 > max_pairs[dev]) cfg.gridDim = dim3(static_cast<unsigned>(2 * max_pairs[dev]));
   }
+  // programmatic dependent launch: the set-up and the weight stream overlap the
+  // previous kernel on the stream; token loads and output stores wait for it
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
@@ -432,9 +440,9 @@ int prefill_grid(const PfParams& p, int sm_count) {
   return 2 * pairs;
 }
 
-cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, cudaStream_t s) {
-  if (swiglu) return xbf16 ? launch_pf<true, true>(p, grid, s) : launch_pf<true, false>(p, grid, s);
-  return xbf16 ? launch_pf<false, true>(p, grid, s) : launch_pf<false, false>(p, grid, s);
+cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s) {
+  if (swiglu) return xbf16 ? launch_pf<true, true>(p, grid, pdl, s) : launch_pf<true, false>(p, grid, pdl, s);
+  return xbf16 ? launch_pf<false, true>(p, grid, pdl, s) : launch_pf<false, false>(p, grid, pdl, s);
 }
 
 }  // namespace kl

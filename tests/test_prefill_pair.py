@@ -87,3 +87,18 @@ def test_repeated_calls_deterministic():
     b = kl.quant_linear(xc, p)
     torch.testing.assert_close(a, b, rtol=0, atol=0)
     assert N.device_status(torch.cuda.current_device()) == 0
+
+
+def test_pdl_chain_reads_previous_output():
+    """With programmatic dependent launch the second GEMM starts while the first
+    runs; its token loads must still see the first GEMM's finished output."""
+    m, n1, k = 1024, 2048, 1024
+    x, p1, q1, s1 = make(m, n1, k, seed=31)
+    _, p2, q2, s2 = make(m, 1024, n1, seed=32)
+    xc = x.cuda()
+    for _ in range(3):
+        y1 = kl.quant_linear(xc, p1, pdl=True)
+        y2 = kl.quant_linear(y1, p2, pdl=True)
+    torch.cuda.synchronize()
+    assert_matches_oracle(y1, ref(x, q1, s1), what="pdl first")
+    assert_matches_oracle(y2, ref(y1.cpu(), q2, s2), what="pdl second")
