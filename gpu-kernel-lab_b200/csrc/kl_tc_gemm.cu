@@ -51,7 +51,7 @@ namespace {
 // region; the epilogue adds the NI partial accumulators.
 template <int NMMA, int KBL>
 struct TcCfg {
-  static constexpr int NI = NMMA <= 32 ? 4 : (NMMA == 64 ? 2 : 1);   // MMA issuer warps
+  static constexpr int NI = NMMA <= 64 ? 2 : 1;                        // MMA issuer warps
   static constexpr int ACOLS = KBL / 2;                      // TMEM columns of one A stage (bf16 pairs)
   static constexpr int D_PITCH = NMMA < 32 ? 32 : NMMA;     // columns per D accumulator
   static constexpr int A_STAGES_FIT = (512 - 2 * NI * D_PITCH) / ACOLS;
@@ -526,20 +526,33 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
       const uint8_t* wstage = smem + L.w + pwc.idx * WSB;
-      uint32_t out[is_w4<FMT>() ? 1 : EPT / 2];
       if constexpr (!is_w4<FMT>()) {
         // EPT int8 = EPT/16 chunks of 16 B; chunk g of the stage row sits in column
-        // block g/8 at position (g%8) ^ (r & 7) (128B swizzle)
+        // block g/8 at position (g%8) ^ (r & 7) (128B swizzle).  All chunks are
+        // loaded first; then each pair of chunks (16 TMEM columns) is converted and
+        // stored, so at most 16 converted words are live at a time.
+        uint4 v[EPT / 16];
 #pragma unroll
         for (int cc = 0; cc < EPT / 16; ++cc) {
           const int g = h * (EPT / 16) + cc;
-          const uint4 v = *reinterpret_cast<const uint4*>(wstage + (g >> 3) * BLK + r * 128 + (((g & 7) ^ (r & 7)) << 4));
-          const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+          v[cc] = *reinterpret_cast<const uint4*>(wstage + (g >> 3) * BLK + r * 128 + (((g & 7) ^ (r & 7)) << 4));
+        }
+        const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
+                                static_cast<uint32_t>(EPT / 2) * h;
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t], out[cc * 8 + 2 * t], out[cc * 8 + 2 * t + 1]);
-            else s8x4_to_f16x4(wd[t], out[cc * 8 + 2 * t], out[cc * 8 + 2 * t + 1]);
+        for (int j = 0; j < EPT / 32; ++j) {
+          uint32_t part[16];
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            const uint4 vv = v[2 * j + c2];
+            const uint32_t wd[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t], part[c2 * 8 + 2 * t], part[c2 * 8 + 2 * t + 1]);
+              else s8x4_to_f16x4(wd[t], part[c2 * 8 + 2 * t], part[c2 * 8 + 2 * t + 1]);
+            }
           }
+          tmem_st16(a_tmem + 16u * j, part);
         }
       } else {
         // EPT nibbles = EPT/32 chunks of 16 B; 64B swizzle: chunk g at g ^ ((r >> 1) & 3)
@@ -569,17 +582,6 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             }
           }
           tmem_st16(a_tmem4 + 16u * cc, part);
-        }
-      }
-      if constexpr (!is_w4<FMT>()) {
-        const uint32_t a_tmem = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
-                                static_cast<uint32_t>(EPT / 2) * h;
-#pragma unroll
-        for (int j = 0; j < EPT / 32; ++j) {
-          uint32_t part[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) part[t] = out[16 * j + t];
-          tmem_st16(a_tmem + 16u * j, part);
         }
       }
       tc_wait_st();
@@ -689,20 +691,17 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, v[j], acc[cb * 16 + j]);
           }
         } else {
-          // two groups per stage: issuers [0, NI/2) hold group 0, [NI/2, NI) group 1
-          static_assert(GPS == 2 && Cfg::NI == 4, "two-group stages use four issuers");
+          // two groups per stage: issuer 0 holds group 0 (K steps 0-7), issuer 1 group 1
+          static_assert(GPS == 2 && Cfg::NI == 2, "two-group stages use one issuer per group");
 #pragma unroll
           for (int cb = 0; cb < NMMA / 16; ++cb) {
+            uint32_t t0[16], t1[16];
+            tmem_ld16(d_tmem + 16u * cb, t0);
+            tmem_ld16(d_tmem + static_cast<uint32_t>(Cfg::D_PITCH) + 16u * cb, t1);
+            tc_wait_ld();
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-              uint32_t t0[16], t1[16];
-              tmem_ld16(d_tmem + static_cast<uint32_t>((2 * gi) * Cfg::D_PITCH) + 16u * cb, t0);
-              tmem_ld16(d_tmem + static_cast<uint32_t>((2 * gi + 1) * Cfg::D_PITCH) + 16u * cb, t1);
-              tc_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                acc[cb * 16 + j] = fmaf(gs[gi], __uint_as_float(t0[j]) + __uint_as_float(t1[j]), acc[cb * 16 + j]);
-            }
+            for (int j = 0; j < 16; ++j)
+              acc[cb * 16 + j] = fmaf(gs[1], __uint_as_float(t1[j]), fmaf(gs[0], __uint_as_float(t0[j]), acc[cb * 16 + j]));
           }
         }
         tc_fence_before();
