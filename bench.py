@@ -13,7 +13,8 @@ rank (synthetic data -- no checkpoints).
             of all ranks / device time of the step (max over ranks), GB/s.
 ``e2e``     the same metric through the public API with host buffers: each step
             copies every GEMM input from pinned host memory and reads the
-            lm_head logits back, inside the timed region.
+            lm_head logits back, inside the timed region (uploads, GEMMs and
+            downloads of different batch sizes overlap on three streams).
 Other workloads (``--workload``): prefill (config 2, TFLOP/s), w4a16 (config 3),
 llama (config 4; ``--lm-head-shard`` vocab-shards the lm_head with an NCCL
 all-gather).
@@ -352,19 +353,53 @@ def bench_decode(args, kl, world, rank, local, dist):
     h2d = sum(t.numel() * 2 for t in pinned.values())
     d2h = sum(t.numel() * 2 for t in head_out.values())
 
+    # Copies run on their own streams so that the upload of one batch size's
+    # activations and the download of another's logits overlap the GEMMs:
+    # upload(M) -> step graph(M) -> download(M), with the next upload into a
+    # buffer waiting for the graph that last read it, and the next graph
+    # waiting for the download of the logits it overwrites.
+    main = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    read_done = {m: None for m in ms_list}      # graph(M) finished reading x_flat[M]
+    out_done = {m: None for m in ms_list}       # download of M's logits finished
+
     def e2e_step():
         for m in ms_list:
-            x_flat[m].copy_(pinned[m], non_blocking=True)
+            with torch.cuda.stream(s_in):
+                if read_done[m] is not None:
+                    s_in.wait_event(read_done[m])
+                x_flat[m].copy_(pinned[m], non_blocking=True)
+                up = torch.cuda.Event()
+                up.record(s_in)
+            main.wait_event(up)
+            if out_done[m] is not None:
+                main.wait_event(out_done[m])
             per_m_graph[m].replay()
-            head_out[m].copy_(passes[m][-1][3], non_blocking=True)
+            ran = torch.cuda.Event()
+            ran.record(main)
+            read_done[m] = ran
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ran)
+                head_out[m].copy_(passes[m][-1][3], non_blocking=True)
+                down = torch.cuda.Event()
+                down.record(s_out)
+            out_done[m] = down
+
+    def join():
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
+    join()
     barrier()
     s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record()
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
     for _ in range(args.steps):
         e2e_step()
+    join()
     t2.record()
     barrier()
     e2e_ms = s2.elapsed_time(t2) / args.steps
