@@ -676,6 +676,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       const uint32_t d_tmem = tmem + lane_base + Cfg::d_col(pd.idx, 0);
       const bool full_tile = seg_end && seg_kb0 == 0 && ce.kb == ce.kb_total - 1;
       float* part_base = nullptr;
+      const int mrem = pr.m - mt * NMMA;      // token columns of this tile that exist
       if (seg_end && !full_tile) {
         const int slot = (ce.tile_u0 == first_tile_u0) ? 0 : 1;
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
@@ -722,7 +723,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
 #pragma unroll
         for (int cb = 0; cb < NMMA / 16; ++cb)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
+          for (int j = 0; j < 16; ++j)
+            if (cb * 16 + j < mrem) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
       } else if constexpr (NMMA <= 64) {
         // Pull the whole accumulator into registers and hand the TMEM buffer
         // back to the MMA issuers before the (slower) global stores.
@@ -748,7 +750,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             E::emit16(pr, mt, nt, r, cb, o, xg, eg);
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[cb * 16 + j];
+            for (int j = 0; j < 16; ++j)
+              if (cb * 16 + j < mrem) part_base[(cb * 16 + j) * 128 + r] = v[cb * 16 + j];
           }
         }
         if (full_tile) continue;
@@ -764,7 +767,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
             E::emit16(pr, mt, nt, r, cb, o, xg, eg);
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) part_base[(cb * 16 + j) * 128 + r] = v[j];
+            for (int j = 0; j < 16; ++j)
+              if (cb * 16 + j < mrem) part_base[(cb * 16 + j) * 128 + r] = v[j];
           }
         }
         tc_fence_before();
@@ -791,19 +795,32 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       __threadfence();
       const float s = grouped<FMT>() ? 1.0f : E::row_scale(pr, prow);
       for (int cb = 0; cb < NMMA / 16; ++cb) {
+        // partials hold only the token columns that exist; the contributors are
+        // summed in CTA order whatever the number of columns
+        const int nv = mrem - cb * 16;
+        if (nv <= 0) break;
         float o[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] = 0.f;
-#pragma unroll 4
-        for (long long cc = c_first; cc <= c_last; ++cc) {
-          // slot 0 holds a contributor's first tile: the one its range starts in
+        // slot 0 holds a contributor's first tile: the one its range starts in
+        auto part_src = [&](long long cc) {
           const int sl = unit_lo(cc, p.units, G) >= ce.tile_u0 ? 0 : 1;
-          const float* src = p.partials + (cc * 2 + sl) * static_cast<long long>(NMMA) * 128 + cb * 16 * 128 + r;
-          float t[16];
+          return p.partials + (cc * 2 + sl) * static_cast<long long>(NMMA) * 128 + cb * 16 * 128 + r;
+        };
+        if (nv == 1) {
+          // one token: eight contributors' loads in flight at a time
+#pragma unroll 8
+          for (long long cc = c_first; cc <= c_last; ++cc) o[0] += __ldcg(part_src(cc));
+        } else {
+#pragma unroll 4
+          for (long long cc = c_first; cc <= c_last; ++cc) {
+            const float* src = part_src(cc);
+            float t[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) t[j] = __ldcg(src + j * 128);
+            for (int j = 0; j < 16; ++j) t[j] = j < nv ? __ldcg(src + j * 128) : 0.f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] += t[j];
+            for (int j = 0; j < 16; ++j) o[j] += t[j];
+          }
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) o[j] *= s;
