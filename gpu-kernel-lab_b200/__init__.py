@@ -20,6 +20,7 @@ from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequanti
                            quantize_int4_asym)
 from .native_ops import dequantize_native
 from .adapters import install_quantized_projections
+from .packed_store import export_packed, install_packed, load_packed, save_packed
 from .sharded_head import VocabShardedHead
 from .kernel_policy import QwenKernelPolicy, load_qwen_policy, select_qwen_policy
 
@@ -30,4 +31,5 @@ __all__ = [
     "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec", "GroupedLinear",
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
     "select_qwen_policy", "sharded_head", "VocabShardedHead",
+    "export_packed", "save_packed", "load_packed", "install_packed", "packed_store",
 ]

@@ -101,14 +101,37 @@ def install_quantized_projections(model, policy=None, *, fmt: str = "w8_row", la
     if head_fmt is not None and head_fmt not in FORMATS:
         raise ValueError(f"unknown lm_head format {head_fmt!r}")
 
+    def quantize(key, dense, f):
+        return QuantLinear.from_weight(dense(), f, group_size)
+
+    return _install(model, plan, head_fmt, quantize)
+
+
+def _install(model, plan: dict, head_fmt, make) -> dict:
+    """Replace the projections named by ``plan`` (layer -> format or None) and
+    the lm_head (``head_fmt``).  ``make(key, dense, fmt)`` returns the
+    :class:`QuantLinear` for one projection; ``key`` is its name in a packed
+    store (``layers.<i>.qkv|o|gate_up|down`` or ``lm_head``) and ``dense()``
+    returns the dense weight it replaces (rows of Q, K, V or gate, up
+    concatenated)."""
+    decoder = model.model.layers
     replaced, packed_bytes, dense_bytes = 0, 0, 0
 
-    def pack(weight, f):
-        nonlocal packed_bytes, dense_bytes
-        q = QuantLinear.from_weight(weight, f, group_size)
+    def pack(key, dense, f, out_features, in_features):
+        nonlocal packed_bytes
+        q = make(key, dense, f)
+        if (q.out_features, q.in_features) != (out_features, in_features):
+            raise ValueError(f"{key}: packed weight is {q.out_features}x{q.in_features}, "
+                             f"the module needs {out_features}x{in_features}")
         packed_bytes += q.weight_q.storage_bytes
-        dense_bytes += weight.numel() * weight.element_size()
         return q
+
+    def released(*modules):
+        nonlocal dense_bytes
+        for m in modules:
+            w = m.weight
+            if w.device.type != "meta":
+                dense_bytes += w.numel() * w.element_size()
 
     with torch.no_grad():
         for index, layer in enumerate(decoder):
@@ -121,29 +144,38 @@ def install_quantized_projections(model, policy=None, *, fmt: str = "w8_row", la
             act = getattr(mlp, "act_fn", None)
             if not isinstance(act, nn.SiLU) and getattr(act, "__class__", type(None)).__name__ not in ("SiLU", "SiLUActivation"):
                 raise ValueError("the fused gate_up epilogue implements SiLU only")
-            sizes = [m.out_features for m in (attn.q_proj, attn.k_proj, attn.v_proj)]
-            in_features = attn.q_proj.in_features
-            fused = _FusedQKV(pack(torch.cat([attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight]), f), sizes)
+            q, k, v = attn.q_proj, attn.k_proj, attn.v_proj
+            sizes = [m.out_features for m in (q, k, v)]
+            in_features = q.in_features
+            qkv = pack(f"layers.{index}.qkv", lambda: torch.cat([q.weight, k.weight, v.weight]), f,
+                       sum(sizes), in_features)
+            gate, up, down, o = mlp.gate_proj, mlp.up_proj, mlp.down_proj, attn.o_proj
+            o_q = pack(f"layers.{index}.o", lambda: o.weight, f, o.out_features, o.in_features)
+            gate_up = pack(f"layers.{index}.gate_up", lambda: torch.cat([gate.weight, up.weight]), f,
+                           gate.out_features + up.out_features, gate.in_features)
+            down_q = pack(f"layers.{index}.down", lambda: down.weight, f, down.out_features, down.in_features)
+            released(q, k, v, o, gate, up, down)
+            fused = _FusedQKV(qkv, sizes)
             attn.kl_qkv = fused.weight
             attn.register_forward_pre_hook(fused.reset)
             attn.q_proj = QKVSlice(fused, 0, in_features)
             attn.k_proj = QKVSlice(fused, 1, in_features)
             attn.v_proj = QKVSlice(fused, 2, in_features)
-            attn.o_proj = pack(attn.o_proj.weight, f)
-            gate_up = pack(torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]), f)
+            attn.o_proj = o_q
             mlp.kl_gate_up = gate_up
             del mlp.gate_proj, mlp.up_proj
-            mlp.down_proj = pack(mlp.down_proj.weight, f)
+            mlp.down_proj = down_q
             mlp.forward = types.MethodType(_mlp_forward, mlp)
             replaced += 7
         if head_fmt is not None:
-            _check_bias_free(model.lm_head)
-            head = model.lm_head.weight
+            lm = model.lm_head
+            _check_bias_free(lm)
+            head = lm.weight
             embed = getattr(getattr(model.model, "embed_tokens", None), "weight", None)
-            tied = embed is not None and head.data_ptr() == embed.data_ptr()
-            model.lm_head = pack(head, head_fmt)
-            if tied:                                  # the embedding still holds the dense matrix
-                dense_bytes -= head.numel() * head.element_size()
+            tied = embed is not None and head.device.type != "meta" and head.data_ptr() == embed.data_ptr()
+            model.lm_head = pack("lm_head", lambda: head, head_fmt, lm.out_features, lm.in_features)
+            if not tied:                              # a tied embedding still holds the dense matrix
+                released(lm)
             replaced += 1
 
     info = {"linear_modules": replaced, "packed_bytes": packed_bytes, "dense_bytes_released": dense_bytes,
