@@ -570,13 +570,130 @@ def bench_prefill(args, kl, world, rank, local, dist):
             "clocks": clocks.summary()}
 
 
+def bench_rmsnorm(args, kl, world, rank, local, dist):
+    """The fused residual-add + RMSNorm in front of each layer's QKV and gate_up
+    (Qwen3-0.6B hidden 1024, bf16).  GB/s = (x, residual, weight read; y and the
+    residual stream written) per launch / device time.  Four buffer sets
+    (268 MB at M = 8192) rotate so that no launch finds its inputs in L2."""
+    import numpy as np
+    import torch
+    from oracle import quant_oracle as O
+    device = torch.device("cuda", local)
+    n = QWEN_LAYER[0][2]
+    ms_list = [int(v) for v in args.batch.split(",")] if args.batch else [1, 64, 8192]
+    hbm, _, _, peak_kind = measured_peaks()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5 + rank)
+    w = torch.randn(n, device=device, generator=gen).to(torch.bfloat16)
+    per_m, total_bytes, total_ms = {}, 0, 0.0
+    with ClockSampler(local) as clocks, torch.inference_mode():
+        for m in ms_list:
+            sets = [tuple(torch.randn(m, n, device=device, generator=gen).to(torch.bfloat16) for _ in range(2))
+                    + tuple(torch.empty(m, n, device=device, dtype=torch.bfloat16) for _ in range(2))
+                    for _ in range(4)]
+
+            def launch(i):
+                x, r, y, c = sets[i % 4]
+                N_ = kl._native
+                N_.check(N_.lib().kl_rmsnorm(N_.ptr(x), N_.ptr(r), N_.ptr(w), N_.KL_DT_BF16, m, n, 1e-6, 0,
+                                             N_.ptr(y), N_.ptr(c), N_.stream_handle(device)))
+
+            reps = 20
+            for i in range(args.warmup):
+                launch(i)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(reps):
+                    launch(i)
+            for _ in range(args.warmup):
+                graph.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / (args.steps * reps)
+            del graph
+            nbytes = 5 * m * n * 2 + 2 * n
+            per_m[str(m)] = {"us": round(ms * 1e3, 3), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                             "frac_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 3)}
+            total_bytes += nbytes
+            total_ms += ms
+            # spot check against the oracle (first rows of the last set)
+            x, r, y, c = sets[(reps - 1) % 4]
+            ey, ec = O.qwen_residual_rmsnorm(x[:4].float().cpu().numpy(), r[:4].float().cpu().numpy(),
+                                             w.float().cpu().numpy())
+            assert np.array_equal(c[:4].float().cpu().numpy(), ec)
+            assert np.allclose(y[:4].float().cpu().numpy(), ey, rtol=2e-2, atol=2e-2)
+            del sets
+    big = str(ms_list[-1])
+    value = world * per_m[big]["GB/s"]
+    # end to end through the public API: host copies of x and residual in, y and the stream out
+    m = ms_list[-1]
+    hx = torch.randn(m, n).to(torch.bfloat16).pin_memory()
+    hr = torch.randn(m, n).to(torch.bfloat16).pin_memory()
+    hy = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    hc = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        with torch.inference_mode():
+            y, c = kl.qwen_residual_rmsnorm(hx.to(device, non_blocking=True), hr.to(device, non_blocking=True),
+                                            w)
+        hy.copy_(y, non_blocking=True)
+        hc.copy_(c, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.steps
+    nbytes = 5 * m * n * 2 + 2 * n
+    # CPU: the reference's eager expression as restated in the oracle, numpy on the host
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        xs = np.random.default_rng(0).standard_normal((min(m, 2048), n)).astype(np.float32)
+        xs, rs, ws = O.bf16_round(xs), O.bf16_round(xs[::-1].copy()), O.bf16_round(np.ones(n, np.float32))
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 5.0:
+            O.qwen_residual_rmsnorm(xs, rs, ws)
+            reps += 1
+        secs = time.perf_counter() - t0
+        cpu = {"value": round(reps * (5 * xs.size * 2 + 2 * n) / secs / 1e9, 3), "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"{xs.shape[0]} x {n} bf16 rows, {reps} calls ({secs:.1f} s)"}
+    return {"metric": "fused residual-add + RMSNorm HBM GB/s (Qwen3-0.6B hidden 1024, bf16)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_m[big]["us"] * 20 / 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "residual + RMSNorm before QKV / gate_up", "batch_m": ms_list,
+                       "n": n, "l2": "4 rotating buffer sets, 268 MB at M=8192 (larger than L2)",
+                       "launch": "20 launches per step in a CUDA graph"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "kernel": "rmsnorm_vec_kernel<bf16, residual>", "achieved": per_m[big]["GB/s"],
+                         "peak": hbm, "unit": "GB/s", "frac": per_m[big]["frac_hbm"], "peak_source": peak_kind,
+                         "traffic": None},
+            "e2e": {"value": round(world * nbytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": 2 * m * n * 2, "d2h_bytes_per_step": 2 * m * n * 2,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 20 * args.steps * len(ms_list),
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "llama", "w4"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "llama", "w4", "rmsnorm"], default="decode")
     ap.add_argument("--batch", default="", help="comma-separated M values (overrides the workload's)")
     ap.add_argument("--swiglu", action="store_true", help="prefill: fuse SwiGLU into gate_up")
     ap.add_argument("--lm-head-shard", action="store_true", help="llama: vocab-shard the lm_head + NCCL all-gather")
@@ -591,14 +708,16 @@ def main():
     try:
         if args.workload == "prefill":
             result = bench_prefill(args, kl, world, rank, local, dist)
+        elif args.workload == "rmsnorm":
+            result = bench_rmsnorm(args, kl, world, rank, local, dist)
         else:
             result = bench_decode(args, kl, world, rank, local, dist)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "prefill":
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("prefill", "rmsnorm"):
             shapes, ms, fmt, _ = workload_of(args)
             v, secs, desc, threads = cpu_path_sample(shapes, ms, fmt, budget_s=10.0)
             result["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                       "sample": desc + f" ({secs:.1f} s)"}
-        elif rank == 0 and world == 1 and not args.no_cpu_baseline:
+        elif rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "prefill":
             result["cpu_baseline"] = None
         if rank == 0:
             print(json.dumps(result), flush=True)

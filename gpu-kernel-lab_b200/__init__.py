@@ -21,6 +21,7 @@ from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequanti
 from .native_ops import dequantize_native
 from .adapters import install_quantized_projections
 from .packed_store import export_packed, install_packed, load_packed, save_packed
+from .rmsnorm import qwen_residual_rmsnorm, qwen_rmsnorm
 from .sharded_head import VocabShardedHead
 from .kernel_policy import QwenKernelPolicy, load_qwen_policy, select_qwen_policy
 
@@ -32,4 +33,5 @@ __all__ = [
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
     "select_qwen_policy", "sharded_head", "VocabShardedHead",
     "export_packed", "save_packed", "load_packed", "install_packed", "packed_store",
+    "qwen_rmsnorm", "qwen_residual_rmsnorm", "rmsnorm",
 ]

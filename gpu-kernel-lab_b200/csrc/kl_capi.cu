@@ -525,6 +525,21 @@ int kl_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, fl
   return e == cudaSuccess ? KL_OK : cuda_fail(e, "top-k merge launch");
 }
 
+int kl_rmsnorm(const void* x, const void* residual, const void* weight, int dtype, int rows, int n, float eps,
+               int precise, void* y, void* residual_out, void* stream) {
+  if (!x || !weight || !y) return fail(KL_ERR_INVALID, "x, weight and y must be non-null");
+  if ((residual == nullptr) != (residual_out == nullptr))
+    return fail(KL_ERR_INVALID, "residual and residual_out must be given together");
+  if (dtype != KL_DT_BF16 && dtype != KL_DT_F16 && dtype != KL_DT_F32) return fail(KL_ERR_INVALID, "unknown dtype %d", dtype);
+  if (rows < 0 || n <= 0 || n > KL_RMSNORM_MAX_N)
+    return fail(KL_ERR_INVALID, "need rows >= 0 and 0 < n <= %d (n=%d)", KL_RMSNORM_MAX_N, n);
+  if (!(eps > 0.0f) || !(eps < 3.0e38f)) return fail(KL_ERR_INVALID, "epsilon must be finite and positive");
+  if (rows == 0) return KL_OK;
+  const cudaError_t e = launch_rmsnorm(x, residual, weight, dtype, rows, n, eps, precise ? 1 : 0, y, residual_out,
+                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KL_OK : cuda_fail(e, "rmsnorm launch");
+}
+
 int kl_quantize_w8_row(const void* w, int w_dtype, int n, int k, int8_t* q, void* scale_bf16, void* stream) {
   if (!w || !q || !scale_bf16) return fail(KL_ERR_INVALID, "null pointer");
   if (n <= 0 || k <= 0) return fail(KL_ERR_INVALID, "weight must be a nonempty [N,K] matrix");

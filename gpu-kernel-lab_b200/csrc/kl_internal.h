@@ -122,6 +122,9 @@ size_t topk_rows_candidate_bytes(int rows, int n, int top_k);
 // packed_out: ids receives (id << 32 | f32 value bits) pairs and values is unused
 cudaError_t launch_topk_rows(const void* logits, bool xbf16, int rows, int n, long long ld, long long index_offset,
                              int top_k, void* cand, float* values, int64_t* ids, cudaStream_t s, bool packed_out);
+// Qwen RMSNorm (kl_rmsnorm.cu); residual/residual_out both null for the plain norm
+cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int dtype, int rows, int n,
+                           float eps, int precise, void* y, void* residual_out, cudaStream_t s);
 cudaError_t launch_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
                                    cudaStream_t s);
 

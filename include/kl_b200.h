@@ -214,6 +214,24 @@ int kl_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k,
                        float* values, int64_t* ids, void* stream);
 
 /*
+ * Qwen RMSNorm of each row of x [rows, n] (bf16, f16 or f32; weight [n] of the
+ * same type), optionally fused with the residual add that precedes it.
+ *
+ * Replaces triton_qwen_rmsnorm and triton_qwen_residual_rmsnorm
+ * (learning/03_rmsnorm/qwen_rmsnorm.py:66-131), with the operation order of
+ * their kernels (:13-51):
+ *   c = T(x + residual), written to residual_out
+ *   y = T(T(c * rsqrt(mean(c^2) + eps)) * weight)
+ * residual and residual_out are both NULL for the plain norm. With precise != 0
+ * the scale is 1/sqrt instead of rsqrt. rows may be 0 (nothing to do). All
+ * buffers are contiguous; y and residual_out must not overlap the inputs.
+ */
+#define KL_RMSNORM_MAX_N 16384
+int kl_rmsnorm(const void* x, const void* residual, const void* weight, int dtype,
+               int rows, int n, float eps, int precise, void* y, void* residual_out,
+               void* stream);
+
+/*
  * Host-only description of the launch plan kl_linear would use on a device
  * with `sm_count` SMs, and a self-check of its work partition (every
  * (tile, k-block) unit covered exactly once, workspace slots in bounds).

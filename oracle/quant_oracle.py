@@ -249,3 +249,30 @@ def topk_lowest_index(logits, k):
     logits = np.asarray(logits, F32)
     order = np.argsort(-logits, kind="stable")[:k]
     return logits[order], order.astype(np.int64)
+
+
+# --------------------------------------------------------------------------- RMSNorm
+def round_to(a, dtype: str) -> np.ndarray:
+    """Round f32 values to ``dtype`` ('bf16', 'f16' or 'f32') and back to f32."""
+    a = np.asarray(a, F32)
+    if dtype == "bf16":
+        return bf16_round(a)
+    if dtype == "f16":
+        return a.astype(np.float16).astype(F32)
+    return a
+
+
+def qwen_rmsnorm(x, weight, eps=1e-6, dtype="bf16") -> np.ndarray:
+    """Qwen RMSNorm of each row, in the order of ``learning/03_rmsnorm/qwen_rmsnorm.py:54-58``:
+    f32 mean of squares, ``x * rsqrt(mean + eps)`` rounded to the dtype, then the
+    dtype product with the weight.  ``x`` and ``weight`` hold values of ``dtype``."""
+    f = np.asarray(x, F32)
+    mean = (f.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(F32)
+    normalized = f * (F32(1) / np.sqrt(mean + F32(eps), dtype=F32))
+    return round_to(np.asarray(weight, F32) * round_to(normalized, dtype), dtype)
+
+
+def qwen_residual_rmsnorm(x, residual, weight, eps=1e-6, dtype="bf16"):
+    """``(rmsnorm(c), c)`` with ``c = dtype(x + residual)`` (``qwen_rmsnorm.py:61-63``)."""
+    c = round_to(np.asarray(x, F32) + np.asarray(residual, F32), dtype)
+    return qwen_rmsnorm(c, weight, eps, dtype), c
