@@ -26,7 +26,7 @@ namespace kl {
 namespace {
 
 constexpr int kNormThreads = 256;
-constexpr int kNormChunks = 8;          // 16-byte chunks per lane (vector path)
+constexpr int kNormChunks = 8;          // most 16-byte chunks per lane (vector path)
 
 template <typename T> KL_DEVICE float to_f(T v);
 template <> KL_DEVICE float to_f<float>(float v) { return v; }
@@ -50,8 +50,10 @@ KL_DEVICE float inv_rms(float sumsq, int n, float eps, int precise) {
   return precise ? 1.0f / sqrtf(var) : rsqrtf(var);
 }
 
-template <typename T, bool RES>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
+// CH = 16-byte chunks per lane: 4 for rows one warp covers with 4 (fewer
+// registers, twice the resident warps), else kNormChunks.
+template <typename T, bool RES, int CH>
+__global__ void __launch_bounds__(kNormThreads, CH == 4 ? 4 : 2) rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
                                                                   const T* __restrict__ w, T* __restrict__ y,
                                                                   T* __restrict__ rout, int rows, int n, float eps,
                                                                   int precise, int wpr) {
@@ -64,14 +66,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const T* __re
   const bool active = row < rows && warp / wpr < rows_per_cta;
   const int chunks = n / E;
   const size_t base = static_cast<size_t>(row) * n;
-  float c[kNormChunks * E];
+  float c[CH * E];
+  uint4 wq[CH];                    // weight chunks, loaded with the row (no second round trip)
   float ss = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kNormChunks; ++k) {
+  for (int k = 0; k < CH; ++k) {
     const int ch = (k * wpr + sub) * 32 + lane;
     if (active && ch < chunks) {
       T xv[E];
       *reinterpret_cast<uint4*>(xv) = __ldcs(reinterpret_cast<const uint4*>(x + base) + ch);
+      wq[k] = __ldg(reinterpret_cast<const uint4*>(w) + ch);
       if constexpr (RES) {
         T rv[E], ov[E];
         *reinterpret_cast<uint4*>(rv) = __ldcs(reinterpret_cast<const uint4*>(r + base) + ch);
@@ -100,11 +104,11 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const T* __re
   if (!active) return;
   const float inv = inv_rms(ss, n, eps, precise);
 #pragma unroll
-  for (int k = 0; k < kNormChunks; ++k) {
+  for (int k = 0; k < CH; ++k) {
     const int ch = (k * wpr + sub) * 32 + lane;
     if (ch < chunks) {
       T wv[E], yv[E];
-      *reinterpret_cast<uint4*>(wv) = __ldg(reinterpret_cast<const uint4*>(w) + ch);
+      *reinterpret_cast<uint4*>(wv) = wq[k];
 #pragma unroll
       for (int e = 0; e < E; ++e) yv[e] = from_f<T>(rnd<T>(c[k * E + e] * inv) * to_f<T>(wv[e]));
       __stcs(reinterpret_cast<uint4*>(y + base) + ch, *reinterpret_cast<const uint4*>(yv));
@@ -151,9 +155,14 @@ cudaError_t launch_norm_t(const void* x, const void* r, const void* w, void* y, 
   if (vec && wpr <= kNormThreads / 32) {
     const int rows_per_cta = (kNormThreads / 32) / wpr;
     const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
-    rmsnorm_vec_kernel<T, RES><<<grid, kNormThreads, 0, s>>>(
-        static_cast<const T*>(x), static_cast<const T*>(r), static_cast<const T*>(w), static_cast<T*>(y),
-        static_cast<T*>(rout), rows, n, eps, precise, wpr);
+    if (wpr == 1 && n <= 32 * 4 * E)
+      rmsnorm_vec_kernel<T, RES, 4><<<grid, kNormThreads, 0, s>>>(
+          static_cast<const T*>(x), static_cast<const T*>(r), static_cast<const T*>(w), static_cast<T*>(y),
+          static_cast<T*>(rout), rows, n, eps, precise, wpr);
+    else
+      rmsnorm_vec_kernel<T, RES, kNormChunks><<<grid, kNormThreads, 0, s>>>(
+          static_cast<const T*>(x), static_cast<const T*>(r), static_cast<const T*>(w), static_cast<T*>(y),
+          static_cast<T*>(rout), rows, n, eps, precise, wpr);
   } else {
     rmsnorm_any_kernel<T, RES><<<rows, kNormThreads, 0, s>>>(
         static_cast<const T*>(x), static_cast<const T*>(r), static_cast<const T*>(w), static_cast<T*>(y),
