@@ -127,6 +127,11 @@ int build_problem(TcProblem& pr, const void* x, int x_dtype, int m, int k, const
   rc = encode_2d(&pr.tmap_x, x_dtype == KL_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                  x, k, m, static_cast<uint64_t>(k) * act_bytes(x_dtype), 64, n_mma, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != KL_OK) return rc;
+  if (w_format == KL_W4_ASYM && kblk == 256) {   // zeros ride with the weight stages (box 8 groups x 64 rows)
+    rc = encode_2d(&pr.tmap_z, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, zeros, k / 128, n, static_cast<uint64_t>(k / 128) * 2,
+                   8, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != KL_OK) return rc;
+  }
   pr.scales = scales;
   pr.zeros = zeros;
   pr.y = y;
@@ -152,9 +157,18 @@ long long problem_units(int m, int n, int k, int n_mma, int kblk, bool swiglu) {
   return tc_problem_tiles(pr, n_mma, kblk, swiglu);
 }
 
+// Whether the two-group 4-bit stages (K block 256) can take this problem: the
+// asymmetric format copies a box of zeros per stage by TMA, which needs 16-byte
+// rows of zeros (K % 1024 == 0) and a 16-byte-aligned zeros pointer.
+bool two_group_ok(int fmt, int k, const void* zeros) {
+  if (k % 256) return false;
+  if (fmt == KL_W4_ASYM) return k % 1024 == 0 && aligned16(zeros);
+  return true;
+}
+
 // K block for one GEMM on this device.
-int choose_kblk_single(int m, int n, int k, int fmt, int n_mma, bool swiglu, int sm_count) {
-  if (is_w4(fmt) && k % 256) return 128;
+int choose_kblk_single(int m, int n, int k, int fmt, int n_mma, bool swiglu, int sm_count, const void* zeros) {
+  if (is_w4(fmt) && !two_group_ok(fmt, k, zeros)) return 128;
   return tc_choose_kblk(fmt, n_mma, problem_units(m, n, k, n_mma, 256, swiglu), sm_count);
 }
 
@@ -220,9 +234,12 @@ size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, 
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;
   const int n_mma = tc_choose_nmma(mm, w_format);
-  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm);
+  // the zeros pointer is not known here: size for whichever K block the call picks
+  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm, nullptr);
   const TcPlan plan = plan_tc(n_mma, kblk, problem_units(mm, n, k, n_mma, kblk, swiglu != 0), w_format, sm);
-  return plan.ok ? plan.workspace : 0;
+  if (!plan.ok) return 0;
+  const TcPlan p128 = plan_tc(n_mma, 128, problem_units(mm, n, k, n_mma, 128, swiglu != 0), w_format, sm);
+  return (p128.ok && p128.workspace > plan.workspace) ? p128.workspace : plan.workspace;
 }
 
 int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
@@ -274,7 +291,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     for (int m0 = 0; m0 < m; m0 += mchunk) {
       const int mm = std::min(mchunk, m - m0);
       const int n_mma = tc_choose_nmma(mm, w_format);
-      const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, di.sm_count);
+      const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, di.sm_count, zeros);
       TcParams p;
       std::memset(&p, 0, sizeof(p));
       const char* xb = static_cast<const char*>(x) + static_cast<size_t>(m0) * k * eb;
@@ -377,9 +394,9 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
   for (int i = 0; i < count; ++i)
     units256 += problem_units(problems[i].m, problems[i].n, problems[i].k, hd->n_mma, 256, swiglu != 0);
   hd->kblk = tc_choose_kblk(w_format, hd->n_mma, units256, sm);
-  if (hd->kblk == 256 && is_w4(w_format)) {   // two 128-groups per stage need K % 256 == 0 everywhere
+  if (hd->kblk == 256 && is_w4(w_format)) {   // two 128-groups per stage: every problem must qualify
     for (int i = 0; i < count; ++i)
-      if (problems[i].k % 256) hd->kblk = 128;
+      if (!two_group_ok(w_format, problems[i].k, problems[i].zeros)) hd->kblk = 128;
   }
   long long units = 0;
   for (int i = 0; i < count; ++i) {
@@ -634,7 +651,7 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
   pr.n = n;
   pr.k = k;
   pr.n_out = swiglu ? n / 2 : n;
-  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm_count);
+  const int kblk = choose_kblk_single(mm, n, k, w_format, n_mma, swiglu != 0, sm_count, nullptr);
   const long long units = tc_problem_tiles(pr, n_mma, kblk, swiglu != 0);
   const TcPlan plan = plan_tc(n_mma, kblk, units, w_format, sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan");

@@ -45,6 +45,7 @@ constexpr int kMaxWStages = 16;
 struct alignas(64) TcProblem {
   CUtensorMap tmap_w;                 // int8 [N, K] (box 128 B x 64 rows) or u8 [N, K/2] (64 B x 64 rows)
   CUtensorMap tmap_x;                 // bf16/f16 [M, K] (box 64 elems x n_mma rows), 128B swizzle
+  CUtensorMap tmap_z;                 // KL_W4_ASYM two-group stages: bf16 zeros [N, K/128] (box 8 x 64 rows)
   const void* scales;                 // KL_W8_ROW: bf16 [N]; KL_W4_*: per group of 128
   const void* zeros;                  // KL_W4_ASYM: bf16 [N, K/128]
   void* y;

@@ -75,11 +75,18 @@ template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL
 // then (optional) a second epilogue group that owns accumulator buffer 1 and
 // finishes every other tile.  The int -> bf16 conversion is latency-bound at
 // two warps per scheduler, so the 256-element stages with small token tiles
-// get four converter warps per scheduler.
+// get four converter warps per scheduler.  For the two-group 4-bit stages the
+// converter warps form CG = 2 groups that take alternate units: one converter
+// pass is latency-bound (shared-memory loads, dependent conversion, tcgen05.st
+// and its wait, then the barrier arrivals, measured at ~1750 cycles per unit
+// with all 16 warps on the same unit and under half the issue slots used), so
+// two units in flight overlap one group's waits with the other's conversion.
 template <int FMT, int NMMA, int KBL>
 struct TcRoles {
   static constexpr int NI = TcCfg<NMMA, KBL>::NI;
   static constexpr int CW = (KBL == 256 && NMMA == 16) ? 16 : 8;
+  static constexpr int CG = (KBL == 256 && NMMA == 16 && (FMT == KL_W4_SYM || FMT == KL_W4_ASYM)) ? 2 : 1;
+  static constexpr int CWG = CW / CG;                       // converter warps per group (per unit)
   static constexpr int CONV0 = 3;
   static constexpr int EPI0_WARP0 = CONV0 + CW;
   static constexpr int ISS1_WARP0 = EPI0_WARP0 + 4;
@@ -87,12 +94,22 @@ struct TcRoles {
   static constexpr int EPI1_WARP0 = ISS1_WARP0 + NI - 1;
   static constexpr int WARPS = EPI1_WARP0 + 4 * (EPI_GROUPS - 1);
   static constexpr int THREADS = WARPS * 32;
-  static constexpr int EPT = KBL / (CW / 4);                // K elements per converter thread and stage
+  static constexpr int EPT = KBL / (CWG / 4);               // K elements per converter thread and stage
 };
 // Weight stage: 128 rows x KBL elements, stored as column blocks of one
 // swizzle span (128 B of int8 / 64 B of packed int4) by 128 rows.
 template <int FMT, int KBL> constexpr int w_row_bytes() { return is_w4<FMT>() ? KBL / 2 : KBL; }
 template <int FMT, int KBL> constexpr int w_stage_bytes() { return 128 * w_row_bytes<FMT, KBL>(); }
+// Two-group asymmetric 4-bit stages also carry the tile's zero points: the W
+// producer copies a box of 8 groups x 128 rows of the bf16 zeros [N, K/128]
+// (two 64-row halves, 1 KB each) behind the weights with the same barrier, so
+// the converters read each row's zero from shared memory instead of walking
+// the units themselves.  Needs K % 1024 == 0 (16-byte rows of zeros).
+template <int FMT, int KBL> constexpr bool zeros_in_stage() { return FMT == KL_W4_ASYM && KBL == 256; }
+constexpr int kZeroStageBytes = 2048;
+template <int FMT, int KBL> constexpr int w_stage_pitch() {
+  return w_stage_bytes<FMT, KBL>() + (zeros_in_stage<FMT, KBL>() ? kZeroStageBytes : 0);
+}
 template <int FMT> constexpr bool grouped() { return is_w4<FMT>(); }
 
 constexpr int kXchFloats = 64 * 16;               // SwiGLU up-value exchange: 64 rows x 16 cols f32
@@ -100,7 +117,7 @@ constexpr int kXchBytes = 2 * kXchFloats * 4;      // one exchange area per epil
 constexpr int kUnitCacheBytes = 8 * kMaxGroup;    // problem unit_begin cache (grouped launches)
 
 struct SmemLayout {
-  uint32_t w, x, xch, ucache, bars, misc, total;
+  uint32_t w, x, xch, ucache, zoff, bars, misc, total;
 };
 __host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a_stages, int sw, int sx) {
   SmemLayout l{};
@@ -108,7 +125,8 @@ __host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a
   l.x = l.w + sw * wsb;
   l.xch = l.x + sx * x_stage;
   l.ucache = l.xch + kXchBytes;
-  l.bars = l.ucache + kUnitCacheBytes;
+  l.zoff = l.ucache + kUnitCacheBytes;       // per weight stage: zero-point offset in its box (4 B each)
+  l.bars = l.zoff + 4 * kMaxWStages;
   // w_full, w_empty [sw]; x_full, x_empty [sx]; a_full, a_empty [A]; d_full, d_empty [2]; done
   l.misc = l.bars + 8 * (2 * sw + 2 * sx + 2 * a_stages + 5);
   l.total = l.misc + 16 + 1024;           // + slack to align the base to 1024 B
@@ -321,6 +339,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
   static_assert(!grouped<FMT>() || KBL == 128 || (KBL == 256 && NMMA == 16), "4-bit group mode: one or two groups of 128 per stage");
   constexpr int WSB = w_stage_bytes<FMT, KBL>();
+  constexpr bool ZST = zeros_in_stage<FMT, KBL>();
+  constexpr int WSP = w_stage_pitch<FMT, KBL>();                // stage pitch: weights (+ zeros)
+  static_assert(WSP % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
   constexpr int ROW_BYTES = w_row_bytes<FMT, KBL>();      // bytes of one tile row per stage
   constexpr int SPAN = (is_w4<FMT>() && KBL == 128) ? 64 : 128;   // swizzle span = TMA box inner bytes
   constexpr int NBLK = ROW_BYTES / SPAN;                  // column blocks per stage
@@ -329,11 +350,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int SW = p.w_stages, SX = p.x_stages;
-  const SmemLayout L = smem_layout(WSB, Cfg::X_STAGE, A, SW, SX);
+  const SmemLayout L = smem_layout(WSP, Cfg::X_STAGE, A, SW, SX);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t s_w = s_base + L.w, s_x = s_base + L.x, s_bars = s_base + L.bars;
   float* xch = reinterpret_cast<float*>(smem + L.xch);
   long long* ucache = reinterpret_cast<long long*>(smem + L.ucache);
+  volatile uint32_t* zoff = reinterpret_cast<volatile uint32_t*>(smem + L.zoff);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc + 4);
   volatile int* fix_flags = reinterpret_cast<volatile int*>(smem + L.misc + 8);   // one per epilogue group
@@ -365,8 +387,11 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   Cursor cw;
   auto issue_w = [&]() {
     const TcProblem& pr = *cw.pr;
-    const uint32_t dst = s_w + pw.idx * WSB;
-    mbar_arrive_expect_tx(w_full(pw.idx), WSB);
+    const uint32_t dst = s_w + pw.idx * WSP;
+    // zeros box: 8 groups from a 16-byte-aligned group index; the stage's pair
+    // starts at (2 kb) & 7 within it (published with the barrier's release)
+    if constexpr (ZST) zoff[pw.idx] = static_cast<uint32_t>((cw.kb * 2) & 7);
+    mbar_arrive_expect_tx(w_full(pw.idx), ZST ? WSB + kZeroStageBytes : WSB);
     const int y0 = SWIGLU ? cw.nt * 64 : cw.nt * 128;
     const int y1 = SWIGLU ? pr.n_out + cw.nt * 64 : cw.nt * 128 + 64;
 #pragma unroll
@@ -374,12 +399,17 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       tma_load_2d(dst + b * BLK, &pr.tmap_w, cw.kb * ROW_BYTES + b * SPAN, y0, w_full(pw.idx));
       tma_load_2d(dst + b * BLK + BLK / 2, &pr.tmap_w, cw.kb * ROW_BYTES + b * SPAN, y1, w_full(pw.idx));
     }
+    if constexpr (ZST) {
+      const int gx = (cw.kb * 2) & ~7;
+      tma_load_2d(dst + WSB, &pr.tmap_z, gx, y0, w_full(pw.idx));
+      tma_load_2d(dst + WSB + kZeroStageBytes / 2, &pr.tmap_z, gx, y1, w_full(pw.idx));
+    }
     cw.next();
   };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), Roles::CW); }
+    for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), Roles::CWG); }
     for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), Cfg::NI); }
-    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), Roles::CW); mbar_init(a_empty(i), Cfg::NI); }
+    for (int i = 0; i < A; ++i) { mbar_init(a_full(i), Roles::CWG); mbar_init(a_empty(i), Cfg::NI); }
     for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), Cfg::NI); mbar_init(d_empty(i), 4); }
     mbar_init(done_bar, Cfg::NI);
     *abort_flag = 0;
@@ -491,11 +521,22 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   } else if (warp < Roles::EPI0_WARP0) {
     // -------------------------------------------------------------- converters
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
-    const int h = (warp - Roles::CONV0) >> 2;   // which slice of the K block
+    const int cg = (warp - Roles::CONV0) / Roles::CWG;          // converter group: units cg, cg + CG, ...
+    const int h = ((warp - Roles::CONV0) % Roles::CWG) >> 2;    // which slice of the K block
     const int r = q * 32 + lane;            // tile row owned by this thread
     Pipe pwc{0, SW, 0}, pa{0, A, 0};
+    // this group's first unit; every pass then steps CG units
+    auto step = [&](Cursor& cu, Pipe* pw, Pipe* pp) {
+#pragma unroll
+      for (int s = 0; s < Roles::CG; ++s) {
+        cu.next();
+        if (pw) pw->next();
+        if (pp) pp->next();
+      }
+    };
     Cursor cc_;
     cc_.init(probs, u_lo, u_hi);
+    for (int s = 0; s < cg; ++s) { cc_.next(); pwc.next(); pa.next(); }
     // 4-bit zero point of this thread's row for a unit (a global load, issued
     // one unit ahead so its latency overlaps the previous unit's conversion)
     auto load_zero = [&](const Cursor& cu) -> float {
@@ -511,21 +552,30 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         return 8.0f;
       }
     };
+    // zeros carried in the stage: this thread's row within the box (two 64-row halves)
+    const uint32_t zrow = static_cast<uint32_t>(r) * 16u;
     float z_cur = 8.0f;
-    if constexpr (is_w4<FMT>()) { if (n_local > 0) z_cur = load_zero(cc_); }
-    for (int i = 0; i < n_local; ++i, cc_.next()) {
+    if constexpr (is_w4<FMT>() && !ZST) { if (cg < n_local) z_cur = load_zero(cc_); }
+    for (int i = cg; i < n_local; i += Roles::CG) {
       float z_next = 8.0f;
-      if constexpr (is_w4<FMT>()) {
-        if (i + 1 < n_local) {
+      if constexpr (is_w4<FMT>() && !ZST) {
+        if (i + Roles::CG < n_local) {
           Cursor nx = cc_;
-          nx.next();
+          step(nx, nullptr, nullptr);
           z_next = load_zero(nx);
         }
       }
       if (!wait_bar(w_full(pwc.idx), pwc.phase, abort_flag, p.status)) break;
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
-      const uint8_t* wstage = smem + L.w + pwc.idx * WSB;
+      const uint8_t* wstage = smem + L.w + pwc.idx * WSP;
+      if constexpr (ZST) {
+        // this slice's group is group h of the stage's pair (EPT = 128 per thread)
+        static_assert(!ZST || Roles::EPT == 128, "one group per converter slice");
+        const uint32_t gi = zoff[pwc.idx] + static_cast<uint32_t>(h);
+        const uint16_t zb = *reinterpret_cast<const uint16_t*>(wstage + WSB + zrow + gi * 2u);
+        z_cur = __uint_as_float(static_cast<uint32_t>(zb) << 16);
+      }
       if constexpr (!is_w4<FMT>()) {
         // EPT int8 = EPT/16 chunks of 16 B; chunk g of the stage row sits in column
         // block g/8 at position (g%8) ^ (r & 7) (128B swizzle).  All chunks are
@@ -591,9 +641,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         mbar_arrive(a_full(pa.idx));
         mbar_arrive(w_empty(pwc.idx));
       }
-      pwc.next();
-      pa.next();
-      z_cur = z_next;
+      step(cc_, &pwc, &pa);
+      if constexpr (!ZST) z_cur = z_next;
     }
   } else {
     // ---------------------------------------------------------------- epilogue
@@ -953,7 +1002,8 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   t.kblk = kblk;
   t.units = units;
   t.grid = static_cast<int>(std::min<long long>(units, sm_count));
-  const int wsb = 128 * (w4 ? kblk / 2 : kblk);
+  // weight stage pitch (the two-group asymmetric 4-bit stages carry their zeros)
+  const int wsb = 128 * (w4 ? kblk / 2 : kblk) + ((fmt == KL_W4_ASYM && kblk == 256) ? kZeroStageBytes : 0);
   const int x_stage = (kblk / 64) * n_mma * 128;
   const int a_stages = tc_a_stages(n_mma, kblk);
   t.x_stages = n_mma == 128 ? 3 : (x_stage > 16384 ? 3 : 4);
