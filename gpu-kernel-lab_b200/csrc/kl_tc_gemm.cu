@@ -75,16 +75,17 @@ template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL
 // then (optional) a second epilogue group that owns accumulator buffer 1 and
 // finishes every other tile.  The int -> bf16 conversion is latency-bound at
 // two warps per scheduler, so the 256-element stages with small token tiles
-// get four converter warps per scheduler.  For the two-group 4-bit stages the
-// converter warps form CG = 2 groups that take alternate units: one converter
-// pass is latency-bound (shared-memory loads, dependent conversion, tcgen05.st
-// and its wait, then the barrier arrivals, measured at ~1750 cycles per unit
-// with all 16 warps on the same unit and under half the issue slots used), so
-// two units in flight overlap one group's waits with the other's conversion.
+// get four converter warps per scheduler.  The two-group 4-bit stages use 8
+// converter warps in CG = 2 groups of 4 that take alternate units, each thread
+// converting a whole 256-wide row of its TMEM lane.  With 16 warps on one unit
+// (768 threads, 80 registers and epilogue spills) a unit took ~1750 cycles and
+// under half the issue slots were used; 512 threads leave every role 128
+// registers, and two units in flight overlap one group's waits with the
+// other's conversion.
 template <int FMT, int NMMA, int KBL>
 struct TcRoles {
   static constexpr int NI = TcCfg<NMMA, KBL>::NI;
-  static constexpr int CW = (KBL == 256 && NMMA == 16) ? 16 : 8;
+  static constexpr int CW = (KBL == 256 && NMMA == 16 && !(FMT == KL_W4_SYM || FMT == KL_W4_ASYM)) ? 16 : 8;
   static constexpr int CG = (KBL == 256 && NMMA == 16 && (FMT == KL_W4_SYM || FMT == KL_W4_ASYM)) ? 2 : 1;
   static constexpr int CWG = CW / CG;                       // converter warps per group (per unit)
   static constexpr int CONV0 = 3;
@@ -569,12 +570,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       if (!wait_bar(a_empty(pa.idx), pa.phase ^ 1u, abort_flag, p.status)) break;
       constexpr int EPT = Roles::EPT;              // elements per thread (a slice of the stage row)
       const uint8_t* wstage = smem + L.w + pwc.idx * WSP;
+      // zero points of the stage's two groups (slices that lie in one group use one)
+      float zg0 = z_cur, zg1 = z_cur;
       if constexpr (ZST) {
-        // this slice's group is group h of the stage's pair (EPT = 128 per thread)
-        static_assert(!ZST || Roles::EPT == 128, "one group per converter slice");
-        const uint32_t gi = zoff[pwc.idx] + static_cast<uint32_t>(h);
-        const uint16_t zb = *reinterpret_cast<const uint16_t*>(wstage + WSB + zrow + gi * 2u);
-        z_cur = __uint_as_float(static_cast<uint32_t>(zb) << 16);
+        const uint32_t zz = *reinterpret_cast<const uint32_t*>(wstage + WSB + zrow + zoff[pwc.idx] * 2u);
+        zg0 = __uint_as_float(zz << 16);
+        zg1 = __uint_as_float(zz & 0xFFFF0000u);
       }
       if constexpr (!is_w4<FMT>()) {
         // EPT int8 = EPT/16 chunks of 16 B; chunk g of the stage row sits in column
@@ -606,9 +607,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         }
       } else {
         // EPT nibbles = EPT/32 chunks of 16 B; 64B swizzle: chunk g at g ^ ((r >> 1) & 3)
-        const float z = z_cur;
-        const uint32_t bias = XBF16 ? pack_bf16x2(-(128.0f + z), -(128.0f + z))
-                                    : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
+        auto bias_of = [&](float z) {
+          return XBF16 ? pack_bf16x2(-(128.0f + z), -(128.0f + z)) : pack_f16x2(-(1024.0f + z), -(1024.0f + z));
+        };
+        const uint32_t bias0 = bias_of(zg0), bias1 = bias_of(zg1);
         constexpr uint32_t magic = XBF16 ? (FMT == KL_W4_SYM ? 0x43084308u : 0x43004300u)
                                          : (FMT == KL_W4_SYM ? 0x64086408u : 0x64006400u);
         // each 16-byte chunk (32 nibbles) is 16 TMEM columns: convert and store it at once
@@ -617,6 +619,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
 #pragma unroll
         for (int cc = 0; cc < EPT / 32; ++cc) {
           const int g = h * (EPT / 32) + cc;
+          // this chunk's group within the stage (32 nibbles per chunk, 128 per group)
+          const uint32_t bias = (KBL == 256 && (g >> 2)) ? bias1 : bias0;
           uint32_t part[16];
           // 64-byte rows (64B swizzle) for 128-wide stages, 128-byte rows (128B swizzle) for 256
           const uint4 v = KBL == 128 ? *reinterpret_cast<const uint4*>(wstage + r * 64 + ((g ^ ((r >> 1) & 3)) << 4))
@@ -954,7 +958,7 @@ int tc_threads(int fmt, int n_mma, int kblk) {
   const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
   if (kblk == 256) {
     switch (n_mma) {
-      case 16: return TcRoles<KL_W8_ROW, 16, 256>::THREADS;
+      case 16: return w4 ? TcRoles<KL_W4_ASYM, 16, 256>::THREADS : TcRoles<KL_W8_ROW, 16, 256>::THREADS;
       case 32: return TcRoles<KL_W8_ROW, 32, 256>::THREADS;
       default: return TcRoles<KL_W8_ROW, 64, 256>::THREADS;
     }
