@@ -86,6 +86,25 @@ def test_plan_partition_w4(kl, m, n, k):
     assert plan["kernel"] == 2 and plan["n_mma"] <= 64
 
 
+def test_plan_w4_two_group_stages(kl):
+    """Two 128-groups per stage (256-wide K blocks) only where the stage can
+    carry its zero points: asymmetric 4-bit needs K % 1024 == 0 (16-byte rows
+    of bf16 zeros for the TMA box); symmetric 4-bit has no zeros and needs
+    K % 256 == 0."""
+    N = kl._native
+    tiles = (151936 + 127) // 128
+    assert N.describe_plan(1, 151936, 2048, N.KL_W4_ASYM)["units"] == tiles * 2048 // 256
+    assert N.describe_plan(1, 151936, 1280, N.KL_W4_ASYM)["units"] == tiles * 1280 // 128
+    assert N.describe_plan(1, 151936, 1280, N.KL_W4_SYM)["units"] == tiles * 1280 // 256
+    # ~128 KB of weights in flight per SM: a zero-carrying stage is 16 KB of
+    # nibbles + 2 KB of zeros, so the ring holds one stage fewer
+    asym = N.describe_plan(1, 151936, 2048, N.KL_W4_ASYM)
+    sym = N.describe_plan(1, 151936, 2048, N.KL_W4_SYM)
+    assert asym["threads"] == sym["threads"] == 512
+    assert sym["stages"] == 128 * 1024 // 16384 and asym["stages"] == 128 * 1024 // (16384 + 2048)
+    assert asym["smem"] <= 227 * 1024 and sym["smem"] <= 227 * 1024
+
+
 @pytest.mark.parametrize("sm", [1, 7, 132, 148, 296])
 def test_plan_partition_odd_grids(kl, sm):
     for n, k in [(17, 128), (1024, 1024), (151936, 1024)]:
