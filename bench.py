@@ -214,8 +214,22 @@ def init_dist(args):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version banner on stdout when the communicator comes
+        # up; send that to stderr so rank 0's stdout stays the one JSON line.
+        # Every rank takes the same steps (init, then one barrier).
+        import ctypes
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            ctypes.CDLL(None).fflush(None)
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
         pg = dist
     return world, rank, local, pg
 
