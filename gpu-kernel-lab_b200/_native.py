@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libkl_b200.so")
 KL_OK, KL_ERR_INVALID, KL_ERR_UNSUPPORTED, KL_ERR_CUDA, KL_ERR_WORKSPACE, KL_ERR_TIMEOUT = range(6)
 KL_DT_BF16, KL_DT_F16, KL_DT_F32 = 0, 1, 2
 KL_W8_ROW, KL_W8_GROUP, KL_W4_SYM, KL_W4_ASYM, KL_BF16_DENSE = range(5)
-KL_FLAG_FORCE_SIMT, KL_FLAG_FORCE_TC, KL_FLAG_PDL, KL_FLAG_Y_TRANSPOSED = 1, 2, 4, 8
+KL_FLAG_FORCE_SIMT, KL_FLAG_FORCE_TC, KL_FLAG_PDL, KL_FLAG_Y_TRANSPOSED, KL_FLAG_PERSISTENT = 1, 2, 4, 8, 16
 
 EXPORTED_SYMBOLS = (
     "kl_linear", "kl_linear_workspace_bytes", "kl_project", "kl_int4_gemv",

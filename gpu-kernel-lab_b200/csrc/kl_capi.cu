@@ -286,6 +286,37 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     return KL_OK;
   }
 
+  if (tc && w_format == KL_W8_ROW && !(flags & KL_FLAG_PERSISTENT)) {
+    // One decode-size linear: the single-tile cluster kernel, whose fixed cost
+    // after the previous kernel in the stream is a fraction of the persistent one's.
+    const ChainPlan cp = plan_chain(m, n, k, swiglu != 0, di.sm_count);
+    if (cp.ok) {
+      ChainParams c;
+      std::memset(&c, 0, sizeof(c));
+      rc = encode_2d(&c.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != KL_OK) return rc;
+      rc = encode_2d(&c.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m,
+                     static_cast<uint64_t>(k) * eb, 64, cp.n_mma, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != KL_OK) return rc;
+      c.scales = scales;
+      c.y = y;
+      c.ldy = transposed ? m : n_out;
+      c.m = m;
+      c.n = n;
+      c.k = k;
+      c.n_out = n_out;
+      c.kb_total = (k + 127) / 128;
+      c.bpc = cp.bpc;
+      c.csize = cp.csize;
+      c.y_transposed = transposed ? 1 : 0;
+      c.status = di.status;
+      const cudaError_t e = launch_chain(c, cp, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
+      if (e == cudaSuccess) return KL_OK;
+      // cudaErrorNotSupported: this device cannot hold a cluster of that size: persistent kernel
+      if (e != cudaErrorNotSupported) return cuda_fail(e, "tcgen05 chain GEMM launch");
+    }
+  }
+
   if (tc) {
     const int mchunk = is_w4(w_format) ? 64 : m;
     for (int m0 = 0; m0 < m; m0 += mchunk) {
@@ -642,6 +673,25 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     if (out[1] % 2 || out[1] > (sm_count & ~1) || out[3] > 227 * 1024)
       return fail(KL_ERR_INVALID, "pair plan out of range");
     return KL_OK;
+  }
+  if (w_format == KL_W8_ROW && !(flags & KL_FLAG_PERSISTENT)) {
+    const ChainPlan cp = plan_chain(m, n, k, swiglu != 0, sm_count);
+    if (cp.ok) {
+      out[0] = 4;
+      out[1] = cp.n_tiles * cp.csize;
+      out[2] = 256;
+      out[3] = cp.smem;
+      out[4] = cp.n_mma;
+      out[5] = cp.bpc;
+      out[6] = cp.n_tiles;
+      out[7] = cp.csize;
+      // every K block owned by exactly one CTA of the cluster, none empty
+      const int kb = (k + 127) / 128;
+      if (cp.csize > kChainMaxCluster || cp.bpc > kChainMaxBlocks || (cp.csize - 1) * cp.bpc >= kb ||
+          cp.csize * cp.bpc < kb || cp.smem > 227 * 1024 || out[1] > 2 * sm_count)
+        return fail(KL_ERR_INVALID, "chain plan out of range");
+      return KL_OK;
+    }
   }
   const int mm = is_w4(w_format) ? std::min(m, 64) : m;
   const int n_mma = tc_choose_nmma(mm, w_format);

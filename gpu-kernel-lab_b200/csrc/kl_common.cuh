@@ -74,6 +74,10 @@ KL_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int3
       " [%0], [%1, {%2, %3}], [%4];"
       :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
 }
+// Prefetch a tile of a tensor into L2 (no shared memory, no completion signal).
+KL_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" :: "l"(map), "r"(x), "r"(y) : "memory");
+}
 KL_DEVICE void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(map) : "memory");
 }
@@ -144,6 +148,31 @@ KL_DEVICE bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
 // All threads of all CTAs of the cluster (start-up / teardown only).
 KL_DEVICE void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of a cluster barrier phase, executed per thread (not warp-aligned):
+// every thread of the cluster arrives once per phase, and waits before arriving again.
+KL_DEVICE void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+KL_DEVICE void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// Arrive without ordering this thread's earlier memory operations (a release at
+// cluster scope waits for all of them).
+KL_DEVICE void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (a bulk copy issued after a barrier).
+KL_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory into another CTA's (cluster address), counted on an
+// mbarrier of the destination CTA (cluster address).
+KL_DEVICE void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(bar_cluster) : "memory");
+}
+// 16-byte store into another CTA's shared memory (cluster address) that counts
+// its bytes on an mbarrier of that CTA (also a cluster address).
+KL_DEVICE void st_async_v4(uint32_t remote_addr, float a, float b, float c, float d, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+               :: "r"(remote_addr), "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(__float_as_uint(c)),
+                  "r"(__float_as_uint(d)), "r"(remote_bar)
+               : "memory");
 }
 KL_DEVICE void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst_smem), "r"(ncols) : "memory");

@@ -85,6 +85,36 @@ int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count);
 TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count);
 cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
+// ---- dependent-chain decode GEMM: one 128-row tile per cluster (kl_tc_chain.cu)
+// For one int8 row-scale linear with M <= 64 launched after the op that
+// produces its input: the CTAs of a cluster split the tile's K range, stream
+// their weights and convert them into tensor memory before the programmatic
+// dependent-launch wait, and reduce the K-split partial sums through
+// distributed shared memory after it.
+constexpr int kChainMaxM = 64;
+constexpr int kChainMaxCluster = 8;   // portable cluster sizes only
+constexpr int kChainMaxBlocks = 8;    // 128-wide K blocks per CTA
+struct ChainParams {
+  CUtensorMap tmap_w;                 // int8 [N, K], box 128 B x 64 rows, 128B swizzle
+  CUtensorMap tmap_x;                 // bf16/f16 [M, K], box 64 elems x n_mma rows, 128B swizzle
+  const void* scales;                 // bf16 [N]
+  void* y;
+  long long ldy;
+  int m, n, k, n_out;
+  int kb_total;                       // 128-wide K blocks of the problem
+  int bpc;                            // K blocks per CTA (the last CTA of a cluster may have fewer)
+  int csize;                          // CTAs per cluster = K splits of a tile
+  int y_transposed;
+  int* status;
+};
+struct ChainPlan {
+  bool ok;
+  int n_mma, bpc, csize, n_tiles, smem;
+};
+ChainPlan plan_chain(int m, int n, int k, bool swiglu, int sm_count);
+cudaError_t launch_chain(const ChainParams& p, const ChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
+                         cudaStream_t s);
+
 // ---- prefill: int8 row-scale GEMM on CTA pairs (kl_tc_prefill.cu)
 constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel
 struct PfParams {

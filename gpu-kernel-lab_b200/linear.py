@@ -54,7 +54,9 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
 
     x: [..., K] bf16/f16 CUDA tensor.  Returns [..., N_out] (N_out = N, or N/2
     with ``swiglu``), or [N_out, M] when ``transposed`` (x flattened to [M, K]).
-    ``path``: None (automatic), "tc" (tcgen05 only) or "simt" (CUDA cores only).
+    ``path``: None (automatic), "tc" (tcgen05 only), "simt" (CUDA cores only) or
+    "persistent" (the persistent stream-K tcgen05 kernel even for a decode-size
+    int8 linear that the single-tile cluster kernel would take).
     ``pdl``: launch with programmatic dependent launch (use inside a chain of
     launches / a CUDA graph to overlap weight prefetch with the previous kernel).
     """
@@ -87,6 +89,10 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
         flags |= N.KL_FLAG_FORCE_TC
     elif path == "simt":
         flags |= N.KL_FLAG_FORCE_SIMT
+    elif path == "persistent":
+        flags |= N.KL_FLAG_FORCE_TC | N.KL_FLAG_PERSISTENT
+    elif path is not None:
+        raise ValueError(f"unknown path {path!r}")
     lib = N.lib()
     with torch.cuda.device(x.device):
         if workspace is None:

@@ -63,6 +63,8 @@ extern "C" {
 #define KL_FLAG_PDL           4 /* launch with programmatic dependent launch (overlaps the
                                    weight prefetch with the previous kernel on the stream) */
 #define KL_FLAG_Y_TRANSPOSED  8 /* write y as [N_out, M] (m contiguous) instead of [M, N_out] */
+#define KL_FLAG_PERSISTENT   16 /* int8 decode (M <= 64): use the persistent stream-K kernel even
+                                   where the single-tile cluster kernel for dependent chains applies */
 
 /*
  * y = x @ dequant(w)^T   (optionally SwiGLU-fused), fp32 accumulation,
@@ -238,7 +240,9 @@ int kl_rmsnorm(const void* x, const void* residual, const void* weight, int dtyp
  * Needs no GPU.  Returns KL_OK and fills `out` (array of 8 ints:
  * kernel, grid, threads, smem bytes,
  * n_mma (tcgen05 token tile), stages, tiles, units); kernel 1 = CUDA-core GEMV,
- * 2 = tcgen05 stream-K GEMM, 3 = tcgen05 CTA-pair prefill GEMM (int8 row scale, M >= 256).
+ * 2 = tcgen05 stream-K GEMM, 3 = tcgen05 CTA-pair prefill GEMM (int8 row scale, M >= 256),
+ * 4 = tcgen05 single-tile cluster GEMM for dependent chains (int8 row scale, M <= 64;
+ * there stages = K blocks of 128 per CTA and units = CTAs per cluster).
  */
 int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags,
                      int sm_count, int* out);

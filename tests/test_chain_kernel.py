@@ -1,0 +1,130 @@
+"""Parity of the single-tile cluster kernel (the decode linear for dependent
+chains, ``kl_describe_plan`` kernel 4) against the oracle and against the
+persistent stream-K kernel it replaces for one decode-size linear.
+
+Same gate as every W8A16 test: outputs within max-abs 2e-2 (one bf16 ulp where
+larger) and relative Frobenius 5e-3 of the fp32-accumulated reference
+(dequantise-then-matmul, ``decode_stage2_benchmark.py:55`` of the reference).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant_oracle as O
+from tests.conftest import assert_matches_oracle, load_kl
+
+kl = load_kl()
+N = kl._native
+pytestmark = pytest.mark.gpu
+
+QWEN = {"qkv": (4096, 1024), "o": (1024, 2048), "gate_up": (6144, 1024), "down": (1024, 3072)}
+
+
+def make(m, n, k, seed=0, dtype=torch.bfloat16):
+    gen = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=gen) * 0.02
+    x = torch.randn(m, k, generator=gen).to(dtype)
+    p = kl.quantize_int8_rowwise(w.cuda())
+    return x, p, p.data.cpu().numpy(), p.scales.float().cpu().numpy()
+
+
+def oracle(x, q, s, swiglu=False):
+    y = O.linear_f32(x.float().numpy(), O.dequantize_int8_rowwise(q, s))
+    return O.swiglu(O.bf16_round(y)) if swiglu else y
+
+
+def kernel_of(m, n, k, swiglu=False, flags=0):
+    return N.describe_plan(m, n, k, N.KL_W8_ROW, swiglu=swiglu, flags=flags,
+                           sm_count=torch.cuda.get_device_properties(0).multi_processor_count)["kernel"]
+
+
+@pytest.mark.parametrize("m", [1, 2, 5, 8, 16, 17, 31, 32, 33, 48, 64])
+@pytest.mark.parametrize("name", list(QWEN))
+def test_config1_shapes(m, name):
+    n, k = QWEN[name]
+    sw = name == "gate_up"
+    assert kernel_of(m, n, k, sw) == 4
+    x, p, q, s = make(m, n, k, seed=m)
+    ref = oracle(x, q, s, sw)
+    y = kl.quant_linear(x.cuda(), p, swiglu=sw)
+    assert_matches_oracle(y, ref, what=f"{name} m={m} chain")
+    # the persistent kernel on the same inputs meets the same gate
+    yp = kl.quant_linear(x.cuda(), p, swiglu=sw, path="persistent")
+    assert_matches_oracle(yp, ref, what=f"{name} m={m} persistent")
+
+
+@pytest.mark.parametrize("m,n,k,sw", [
+    (1, 17, 128, False),        # one K block, one partial tile, cluster of 1
+    (3, 129, 1040, False),      # K not a multiple of 128: zero-filled last block
+    (7, 1000, 1040, True),      # SwiGLU with a partial last gate tile
+    (9, 200, 256, True),        # two K blocks, one CTA
+    (64, 3072, 3072, False),    # Llama o: three blocks per CTA
+    (33, 384, 4096, False),     # clusters of 8 with four blocks per CTA
+])
+def test_ragged_shapes(m, n, k, sw):
+    assert kernel_of(m, n, k, sw) == 4
+    x, p, q, s = make(m, n, k, seed=n + k)
+    assert_matches_oracle(kl.quant_linear(x.cuda(), p, swiglu=sw), oracle(x, q, s, sw), what=f"{m}x{n}x{k} sw={sw}")
+
+
+def test_f16_and_transposed():
+    m, n, k = 12, 4096, 1024
+    x, p, q, s = make(m, n, k, seed=3, dtype=torch.float16)
+    ref = oracle(x, q, s)
+    y = kl.quant_linear(x.cuda(), p)
+    assert y.dtype == torch.float16
+    assert_matches_oracle(y, ref, what="f16")
+    yt = kl.quant_linear(x.cuda(), p, transposed=True)
+    assert yt.shape == (n, m)
+    torch.testing.assert_close(yt.T, y, rtol=0, atol=0)
+
+
+def test_deterministic():
+    """K-split partial sums are added in cluster-rank order: bit-identical runs."""
+    x, p, _, _ = make(40, 1024, 3072, seed=9)
+    xc = x.cuda()
+    a = kl.quant_linear(xc, p)
+    for _ in range(3):
+        torch.testing.assert_close(kl.quant_linear(xc, p), a, rtol=0, atol=0)
+
+
+def test_dependent_chain_in_graph():
+    """A model-forward pattern: every linear reads the previous one's output,
+    all launched with programmatic dependent launch and captured in one CUDA
+    graph; the replay equals eager execution and the oracle run in sequence."""
+    m = 4
+    dims = [1024, 4096, 1024, 3072, 1024, 2048, 1024]
+    layers = [make(1, dims[i + 1], dims[i], seed=20 + i) for i in range(len(dims) - 1)]
+    gen = torch.Generator().manual_seed(1)
+    x0 = (torch.randn(m, dims[0], generator=gen)).bfloat16()
+    bufs = [x0.cuda()] + [torch.empty(m, d, dtype=torch.bfloat16, device="cuda") for d in dims[1:]]
+
+    def forward():
+        for i, (_, p, _, _) in enumerate(layers):
+            kl.quant_linear(bufs[i], p, out=bufs[i + 1], pdl=True)
+
+    forward()
+    torch.cuda.synchronize()
+    eager = bufs[-1].clone()
+    # oracle in sequence, each step rounded to bf16 like the kernel output
+    h = x0.float().numpy()
+    for i, (_, _, q, s) in enumerate(layers):
+        ref = O.linear_f32(h, O.dequantize_int8_rowwise(q, s))
+        assert_matches_oracle(bufs[i + 1], ref, what=f"chain step {i}")
+        h = O.bf16_round(bufs[i + 1].float().cpu().numpy())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        forward()
+    bufs[-1].zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(bufs[-1], eager, rtol=0, atol=0)
+
+
+def test_persistent_flag_and_large_problems():
+    """KL_FLAG_PERSISTENT keeps the stream-K kernel; problems too large for one
+    cluster per tile (the 151,936-row lm_head) stay on it automatically."""
+    assert kernel_of(1, 4096, 1024, flags=N.KL_FLAG_PERSISTENT) == 2
+    assert kernel_of(1, 151936, 1024) == 2
+    assert kernel_of(65, 4096, 1024) == 2
+    assert N.device_status(0) == 0

@@ -53,20 +53,73 @@ def test_validation_needs_no_gpu(kl):
     assert lib.kl_int4_gemv(fake, 0, 128, fake, fake, 8, 128, 24, fake, None) == N.KL_ERR_INVALID
 
 
+def chain_plan(m, n, k, swiglu=False, sm=148):
+    """Restatement of the host planner of the single-tile cluster kernel: the
+    fewest 128-wide K blocks per CTA from 2 to 4 that keep the cluster portable
+    (<= 8 CTAs) and the grid within one CTA per SM (two for 64-token tiles),
+    else within two; None where it does not apply (M > 64, or a problem large
+    enough for the persistent kernel)."""
+    if m > 64:
+        return None
+    tiles = (n // 2 + 63) // 64 if swiglu else (n + 127) // 128
+    kb = (k + 127) // 128
+    caps = (2 * sm,) if m > 32 else (sm, 2 * sm)
+    for cap in caps:
+        for bpc in range(2, 5):
+            csize = -(-kb // bpc)
+            if csize <= 8 and tiles * csize <= cap:
+                bpc = min(bpc, kb)
+                return {"tiles": tiles, "bpc": bpc, "csize": -(-kb // bpc)}
+    return None
+
+
 @pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 256, 512, 2048, 8192])
 @pytest.mark.parametrize("n,k", QWEN + LLAMA)
 def test_plan_partition_w8(kl, m, n, k):
-    plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, sm_count=148)
+    N = kl._native
+    plan = N.describe_plan(m, n, k, N.KL_W8_ROW, sm_count=148)
+    chain = chain_plan(m, n, k)
     # M >= 256 with K a multiple of 64 runs on the CTA-pair prefill kernel
-    assert plan["kernel"] == (3 if m >= 256 and k % 64 == 0 else 2)
-    assert 1 <= plan["grid"] <= 148
-    assert plan["smem"] <= 227 * 1024
-    assert plan["n_mma"] in (16, 32, 64, 128, 192)
-    if m <= 64:
-        assert plan["stages"] >= 3          # weight ring of >= 3 stages (16-32 KB each) per SM
-    if plan["kernel"] == 3:
-        assert plan["grid"] % 2 == 0 and plan["n_mma"] == 192
+    if m >= 256 and k % 64 == 0:
+        assert plan["kernel"] == 3
+        assert plan["grid"] % 2 == 0 and plan["n_mma"] == 192 and 1 <= plan["grid"] <= 148
         assert plan["tiles"] == ((n + 255) // 256) * ((m + 191) // 192)
+    elif chain is not None:
+        # one decode linear small enough for the single-tile cluster kernel
+        assert plan["kernel"] == 4
+        assert plan["grid"] == chain["tiles"] * chain["csize"] <= 2 * 148 and chain["csize"] <= 8
+        assert (plan["tiles"], plan["stages"], plan["units"]) == (chain["tiles"], chain["bpc"], chain["csize"])
+        assert plan["n_mma"] == (16 if m <= 16 else 32 if m <= 32 else 64)
+        # two CTAs per SM fit (shared memory) at two K blocks per CTA
+        if plan["stages"] <= 2:
+            assert 2 * plan["smem"] <= 228 * 1024
+    else:
+        assert plan["kernel"] == 2
+    # the persistent stream-K kernel's plan, also taken with KL_FLAG_PERSISTENT
+    if m <= 64:
+        plan = N.describe_plan(m, n, k, N.KL_W8_ROW, flags=N.KL_FLAG_PERSISTENT, sm_count=148)
+        assert plan["kernel"] == 2
+        assert 1 <= plan["grid"] <= 148
+        assert plan["smem"] <= 227 * 1024
+        assert plan["n_mma"] in (16, 32, 64)
+        assert plan["stages"] >= 3          # weight ring of >= 3 stages (16-32 KB each) per SM
+
+
+def test_chain_plan_config1_shapes(kl):
+    """Clusters of the Qwen3-0.6B decode linears: QKV splits K four ways (2
+    blocks per CTA), o eight ways (2 blocks), down eight ways (3 blocks);
+    gate_up three ways (3 blocks, 144 CTAs) up to 32 tokens and four ways (2
+    blocks, 192 CTAs) for 64-token tiles; the lm_head is too large and streams
+    through the persistent kernel."""
+    N = kl._native
+    expect = {(4096, 1024, False): (32, 4, 4), (1024, 2048, False): (8, 8, 8), (6144, 1024, True): (48, 3, 4),
+              (1024, 3072, False): (8, 8, 8)}
+    for (n, k, sw), (tiles, csize, csize64) in expect.items():
+        for m in (1, 8, 32, 64):
+            plan = N.describe_plan(m, n, k, N.KL_W8_ROW, swiglu=sw, sm_count=148)
+            want = csize64 if m > 32 else csize
+            assert plan["kernel"] == 4 and (plan["tiles"], plan["units"]) == (tiles, want), (n, k, m, plan)
+    assert N.describe_plan(1, 151936, 1024, N.KL_W8_ROW, sm_count=148)["kernel"] == 2
 
 
 @pytest.mark.parametrize("m", [1, 16, 64, 512, 8192])
@@ -75,6 +128,8 @@ def test_plan_partition_swiglu(kl, m, n, k):
     plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, swiglu=True, sm_count=148)
     if m >= 256:
         assert plan["kernel"] == 3 and plan["tiles"] == ((n // 2 + 127) // 128) * ((m + 191) // 192)
+    elif chain_plan(m, n, k, swiglu=True) is not None:
+        assert plan["kernel"] == 4 and plan["tiles"] == (n // 2 + 63) // 64
     else:
         assert plan["kernel"] == 2 and plan["tiles"] == ((n // 2 + 63) // 64) * ((m + plan["n_mma"] - 1) // plan["n_mma"])
 
