@@ -1,26 +1,34 @@
 """Benchmark of the W8A16 quantized linear layer on B200 (BASELINE.json metric).
 
-Default workload: the full Qwen3-0.6B decode-step
-projection set -- 28 layers x {fused QKV 4096x1024, o 1024x2048, fused gate_up
-6144x1024, down 1024x3072} + lm_head 151936x1024 = 113 GEMMs, int8 weights with
-per-row bf16 scales (~0.6 GB streamed per pass) -- at batch M in {1, 8, 32, 64}.
-One step = one pass at every M (4 x 113 launches), replayed from CUDA graphs
-whose kernels are chained with programmatic dependent launch.  Weights: random
+Headline: the full Qwen3-0.6B decode-step projection
+set -- 28 layers x {fused QKV 4096x1024, o 1024x2048, fused gate_up 6144x1024,
+down 1024x3072} + lm_head 151936x1024 = 113 GEMMs, int8 weights with per-row
+bf16 scales (~0.6 GB streamed per pass) -- at batch M in {1, 8, 32, 64}.  One
+pass = the 113 GEMMs at every M, each M as one grouped persistent launch; one
+timed step = ``passes_per_step`` passes back to back in one CUDA graph, sized
+so that the timed steps last at least half a second.  Weights: random
 N(0, 0.02), seeded, quantised on the GPU; activations N(0, 1) bf16, seeded per
 rank (synthetic data -- no checkpoints).
 
 ``value``   algorithmic HBM bytes (int8 weights + bf16 scales + bf16 x + bf16 y)
-            of all ranks / device time of the step (max over ranks), GB/s.
+            of all ranks / device time of the timed steps (max over ranks), GB/s.
+``per_m``   per batch size: the grouped launch, and the same 113 GEMMs launched
+            one by one in model order (``chain``: every launch a dependent one,
+            programmatic dependent launch, one CUDA graph) -- the call pattern of
+            a model forward through the drop-in op.
 ``e2e``     the same metric through the public API with host buffers: each step
-            copies every GEMM input from pinned host memory and reads the
-            lm_head logits back, inside the timed region (uploads, GEMMs and
-            downloads of different batch sizes overlap on three streams).
-Other workloads (``--workload``): prefill (config 2, TFLOP/s), w4a16 (config 3),
-llama (config 4; ``--lm-head-shard`` vocab-shards the lm_head with an NCCL
-all-gather).
+            copies every GEMM input from pinned host memory and reads the lm_head
+            logits back, inside the timed region; ``host_link`` times the same
+            copies alone.
+The default run also measures the other BASELINE configs, each as its own key:
+``config0`` (one gate_proj-shaped linear, M = 1), ``prefill`` (config 2, the
+28 layers' GEMMs at M in {512, 2048, 8192}, TFLOP/s, with and without the
+SwiGLU epilogue), ``w4`` (config 3, 4-bit asymmetric group-128) and ``llama``
+(config 4, Llama-3.2-3B shapes at M in {1, 64, 256}; vocab-sharded lm_head
+with an NCCL all-gather when N > 1).  ``--workload`` runs one of them alone.
 
 ``--impl reference`` times the reference's CPU path (dequantise-then-matmul,
-restated in ``oracle/``) on the host cores for the same metric.
+restated in ``oracle/``) on all host cores for the same metric.
 """
 from __future__ import annotations
 
@@ -75,7 +83,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -182,10 +190,13 @@ def run_reference(args):
     shapes, ms, fmt, wdesc = workload_of(args)
     per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
     vals = []
-    for i in range(args.warmup + args.steps):
-        v, _, desc, threads = cpu_path_sample(shapes, ms, fmt, budget_s=per_step, seed=i)
-        if i >= args.warmup:
-            vals.append(v)
+    # every host core, whatever the launcher set (torchrun exports OMP_NUM_THREADS=1)
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(limits=os.cpu_count()):
+        for i in range(args.warmup + args.steps):
+            v, _, desc, threads = cpu_path_sample(shapes, ms, fmt, budget_s=per_step, seed=i)
+            if i >= args.warmup:
+                vals.append(v)
     value = statistics.mean(vals)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -251,11 +262,150 @@ def build_weights(kl, shapes, layers, device, seed=1234, fmt="w8_row"):
     return weights
 
 
+def capture(fn):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def timed(graph, reps, warm=3):
+    """Average device time (ms) of ``reps`` back-to-back replays, after ``warm``."""
+    import torch
+    for _ in range(warm):
+        graph.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def max_over_ranks(v, dist, device):
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+class DecodeSet:
+    """One projection set (GEMMs of every layer + the lm_head) at each batch size:
+    per-M activation buffers (views of one contiguous buffer per M), outputs,
+    the grouped launch and the dependent chain."""
+
+    def __init__(self, kl, weights, ms_list, device, seed):
+        import torch
+        self.kl, self.weights, self.ms_list = kl, weights, ms_list
+        xg = torch.Generator(device=device)
+        xg.manual_seed(seed)
+        self.passes, self.x_flat = {}, {}
+        for m in ms_list:
+            total = sum(m * p.shape[1] for _, p in weights)
+            flat = torch.randn(total, device=device, generator=xg).to(torch.bfloat16)
+            self.x_flat[m] = flat
+            items, off = [], 0
+            for name, p in weights:
+                n, k = p.shape
+                x = flat[off: off + m * k].view(m, k)
+                off += m * k
+                items.append((name, p, x, torch.empty(m, n, device=device, dtype=torch.bfloat16)))
+            self.passes[m] = items
+        self.grouped = {m: kl.GroupedLinear([(x, p, y) for _, p, x, y in self.passes[m]]) for m in ms_list}
+        for m in ms_list:              # eager warm-up (allocates the workspace before capture)
+            self.run_grouped(m)
+            self.run_chain(m)
+        torch.cuda.synchronize()
+
+    def run_grouped(self, m):
+        self.grouped[m].run(pdl=True)
+
+    def run_chain(self, m):
+        for name, p, x, y in self.passes[m]:
+            self.kl.quant_linear(x, p, out=y, pdl=True)
+
+    def pass_bytes(self, m):
+        # weights + their scales (and zeros) + activations in + outputs
+        return sum(p.storage_bytes + 2 * x.numel() + 2 * y.numel() for _, p, x, y in self.passes[m])
+
+    def per_m(self, hbm, reps, device, dist):
+        out = {}
+        for m in self.ms_list:
+            gg, gc = capture(lambda m=m: self.run_grouped(m)), capture(lambda m=m: self.run_chain(m))
+            t_g = max_over_ranks(timed(gg, reps), dist, device)
+            t_c = max_over_ranks(timed(gc, reps), dist, device)
+            del gg, gc
+            b = self.pass_bytes(m)
+            out[str(m)] = {"grouped_ms": round(t_g, 4), "grouped_GB/s": round(b / (t_g * 1e-3) / 1e9, 1),
+                           "frac_hbm": round(b / (t_g * 1e-3) / 1e9 / hbm, 3),
+                           "chain_ms": round(t_c, 4), "chain_GB/s": round(b / (t_c * 1e-3) / 1e9, 1),
+                           "chain_frac_hbm": round(b / (t_c * 1e-3) / 1e9 / hbm, 3),
+                           "tokens/s": round(m / (t_c * 1e-3), 1)}
+        return out
+
+    def head_alone(self, hbm, device):
+        """The largest single GEMM (the lm_head) at the first batch size, graph-timed."""
+        name, p, x, y = self.passes[self.ms_list[0]][-1]
+        g = capture(lambda: [self.kl.quant_linear(x, p, out=y, pdl=True) for _ in range(5)])
+        ms = timed(g, 4) / 5
+        m0 = self.ms_list[0]
+        n, k = p.shape
+        gbs = (p.storage_bytes + 2 * m0 * k + 2 * m0 * n) / (ms * 1e-3) / 1e9
+        return {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "m": m0}
+
+
+def sharded_head_section(kl, full, ms_list, x_of, world, rank, device, dist, steps, fmt="w8_row"):
+    """Vocab-sharded lm_head: the shard GEMM + NCCL all-gather of the logits, and
+    the top-8 alternative (shard GEMM, local top-8, all-gather of candidates,
+    merge), each captured once and replayed; max over ranks."""
+    import torch
+    vocab = full.shape[0]
+    lo, hi = kl.sharded_head.shard_bounds(vocab, world, rank)
+    if fmt == "w4_asym":
+        shard = kl.PackedInt4Asym(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous(),
+                                  full.zeros[lo:hi].contiguous(), full.group_size)
+    else:
+        shard = kl.RowwiseInt8(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous())
+    shead = kl.VocabShardedHead(shard, vocab)
+    res = {"vocab": vocab, "ranks": world, "rows_per_rank": hi - lo, "per_m": {}}
+    reps = max(5, steps)
+
+    class _One:                          # a single rank without a process group
+        @staticmethod
+        def barrier():
+            torch.cuda.synchronize()
+    dist = dist if dist is not None else _One
+    for m in ms_list:
+        x = x_of(m)
+        gathered = torch.empty(vocab, m, dtype=torch.bfloat16, device=device)
+        for _ in range(3):
+            shead(x, gathered=gathered)
+        dist.barrier()
+        sg = capture(lambda: shead(x, gathered=gathered))
+        dist.barrier()
+        t = max_over_ranks(timed(sg, reps), dist if world > 1 else None, device)
+        del sg
+        for _ in range(3):
+            shead.topk(x, 8)
+        dist.barrier()
+        tg = capture(lambda: shead.topk(x, 8))
+        dist.barrier()
+        tk = max_over_ranks(timed(tg, reps), dist if world > 1 else None, device)
+        del tg
+        res["per_m"][str(m)] = {"ms": round(t, 4), "allgather_bytes": vocab * m * 2,
+                                "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1),
+                                "top8_ms": round(tk, 4), "top8_gather_bytes": world * m * 8 * 8}
+    return res
+
+
 def bench_decode(args, kl, world, rank, local, dist):
-    """Config 1 (or 4 with --workload llama): every projection of the decode step
-    at each batch size M.  The step runs each M as ONE grouped tcgen05 launch
-    over all 113 (independent) GEMMs; the same GEMMs launched one by one in
-    model order (PDL-chained CUDA graph) are reported as ``chain``."""
+    """Config 1 (or 4 with --workload llama, 3 with --workload w4): every
+    projection of the decode step at each batch size M, the grouped launch per M
+    as the timed step, the dependent chain per M alongside."""
     import torch
     device = torch.device("cuda", local)
     layer, head = (LLAMA_LAYER, LLAMA_HEAD) if args.workload == "llama" else (QWEN_LAYER, QWEN_HEAD)
@@ -267,105 +417,47 @@ def bench_decode(args, kl, world, rank, local, dist):
     weights.append(("lm_head", quantize(kl, hw, fmt)))
     del hw
     torch.cuda.empty_cache()
-
-    xg = torch.Generator(device=device)
-    xg.manual_seed(99 + rank)
-    passes, x_flat = {}, {}
-    for m in ms_list:
-        # every GEMM's activations are a view of one contiguous buffer per M, so
-        # the end-to-end step moves them from the host in a single copy
-        total = sum(m * p.shape[1] for _, p in weights)
-        flat = torch.randn(total, device=device, generator=xg).to(torch.bfloat16)
-        x_flat[m] = flat
-        items, off = [], 0
-        for name, p in weights:
-            n, k = p.shape
-            x = flat[off: off + m * k].view(m, k)
-            off += m * k
-            y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-            items.append((name, p, x, y))
-        passes[m] = items
-
-    def pass_bytes(m):
-        # weights + their scales (and zeros) + activations in + outputs
-        return sum(p.storage_bytes + 2 * m * x.shape[1] + 2 * m * y.shape[1] for _, p, x, y in passes[m])
-
-    grouped = {m: kl.GroupedLinear([(x, p, y) for _, p, x, y in passes[m]]) for m in ms_list}
-
-    def run_grouped(m):
-        grouped[m].run(pdl=True)
-
-    def run_chain(m):
-        for name, p, x, y in passes[m]:
-            kl.quant_linear(x, p, out=y, pdl=True)
-
-    for m in ms_list:                 # eager warm-up (allocates the workspace before capture)
-        run_grouped(m)
-        run_chain(m)
-    torch.cuda.synchronize()
-
-    def capture(fn):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        return g
-
-    step_graph = capture(lambda: [run_grouped(m) for m in ms_list])
-    per_m_graph = {m: capture(lambda m=m: run_grouped(m)) for m in ms_list}
-    chain_graph = {m: capture(lambda m=m: run_chain(m)) for m in ms_list}
-    torch.cuda.synchronize()
+    ds = DecodeSet(kl, weights, ms_list, device, 99 + rank)
+    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def timed(graph, reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            graph.replay()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / reps
-
+    # one pass = every M once; a timed step = `passes` passes in one graph, so
+    # that the timed steps take at least half a second
+    one = capture(lambda: [ds.run_grouped(m) for m in ms_list])
+    t_pass = max_over_ranks(timed(one, 5), dist, device)
+    del one
+    passes = max(1, int(-(-500.0 // (args.steps * t_pass))))
+    step_graph = capture(lambda: [ds.run_grouped(m) for _ in range(passes) for m in ms_list])
+    torch.cuda.synchronize()
     for _ in range(args.warmup):
         step_graph.replay()
     barrier()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        time.sleep(0.3)
         barrier()
         start.record()
         for _ in range(args.steps):
             step_graph.replay()
         stop.record()
         barrier()
-    ms_step = start.elapsed_time(stop) / args.steps
-    if dist is not None:
-        t = torch.tensor([ms_step], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step = t.item()
-    step_bytes = sum(pass_bytes(m) for m in ms_list)
+    ms_step = max_over_ranks(start.elapsed_time(stop) / args.steps, dist, device)
+    del step_graph
+    step_bytes = passes * sum(ds.pass_bytes(m) for m in ms_list)
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
-
-    hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
-    per_m = {}
-    for m in ms_list:
-        t_g = timed(per_m_graph[m], max(3, args.steps // 2))
-        t_c = timed(chain_graph[m], max(3, args.steps // 2))
-        b = pass_bytes(m)
-        per_m[str(m)] = {"grouped_ms": round(t_g, 4), "grouped_GB/s": round(b / (t_g * 1e-3) / 1e9, 1),
-                         "frac_hbm": round(b / (t_g * 1e-3) / 1e9 / hbm, 3),
-                         "chain_ms": round(t_c, 4), "chain_GB/s": round(b / (t_c * 1e-3) / 1e9, 1)}
+    per_m = ds.per_m(hbm, max(5, args.steps // 2), device, dist)
 
     # ---- e2e through the public API with host buffers
-    pinned = {m: torch.empty(x_flat[m].shape, dtype=x_flat[m].dtype, pin_memory=True).copy_(x_flat[m])
+    pinned = {m: torch.empty(ds.x_flat[m].shape, dtype=torch.bfloat16, pin_memory=True).copy_(ds.x_flat[m])
               for m in ms_list}
-    head_out = {m: torch.empty(passes[m][-1][3].shape, dtype=torch.bfloat16, pin_memory=True) for m in ms_list}
-    h2d = sum(t.numel() * 2 for t in pinned.values())
-    d2h = sum(t.numel() * 2 for t in head_out.values())
+    head_out = {m: torch.empty(ds.passes[m][-1][3].shape, dtype=torch.bfloat16, pin_memory=True) for m in ms_list}
+    h2d = passes * sum(t.numel() * 2 for t in pinned.values())
+    d2h = passes * sum(t.numel() * 2 for t in head_out.values())
+    per_m_graph = {m: capture(lambda m=m: ds.run_grouped(m)) for m in ms_list}
 
     # Copies run on their own streams so that the upload of one batch size's
     # activations and the download of another's logits overlap the GEMMs:
@@ -377,12 +469,12 @@ def bench_decode(args, kl, world, rank, local, dist):
     read_done = {m: None for m in ms_list}      # graph(M) finished reading x_flat[M]
     out_done = {m: None for m in ms_list}       # download of M's logits finished
 
-    def e2e_step():
+    def e2e_pass():
         for m in ms_list:
             with torch.cuda.stream(s_in):
                 if read_done[m] is not None:
                     s_in.wait_event(read_done[m])
-                x_flat[m].copy_(pinned[m], non_blocking=True)
+                ds.x_flat[m].copy_(pinned[m], non_blocking=True)
                 up = torch.cuda.Event()
                 up.record(s_in)
             main.wait_event(up)
@@ -394,7 +486,7 @@ def bench_decode(args, kl, world, rank, local, dist):
             read_done[m] = ran
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ran)
-                head_out[m].copy_(passes[m][-1][3], non_blocking=True)
+                head_out[m].copy_(ds.passes[m][-1][3], non_blocking=True)
                 down = torch.cuda.Event()
                 down.record(s_out)
             out_done[m] = down
@@ -404,95 +496,50 @@ def bench_decode(args, kl, world, rank, local, dist):
         main.wait_stream(s_out)
 
     for _ in range(max(1, args.warmup)):
-        e2e_step()
+        e2e_pass()
     join()
     barrier()
     s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record()
     s_in.wait_stream(main)
     s_out.wait_stream(main)
-    for _ in range(args.steps):
-        e2e_step()
+    for _ in range(args.steps * passes):
+        e2e_pass()
     join()
     t2.record()
     barrier()
-    e2e_ms = s2.elapsed_time(t2) / args.steps
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
+    e2e_ms = max_over_ranks(s2.elapsed_time(t2) / args.steps, dist, device)
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
 
-    # ---- the largest single GEMM alone (lm_head, M = first batch size), graph-timed
-    name, p, x, y = passes[ms_list[0]][-1]
-    head_graph = capture(lambda: [kl.quant_linear(x, p, out=y, pdl=True) for _ in range(5)])
-    head_ms = timed(head_graph, 4) / 5
-    n, k = p.shape
-    m0 = ms_list[0]
-    head_gbs = (p.storage_bytes + 2 * m0 * k + 2 * m0 * n) / (head_ms * 1e-3) / 1e9
+    # the same host copies alone (every rank at once), one direction at a time
+    def copies(direction):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record()
+        for _ in range(passes):
+            for m in ms_list:
+                if direction == "h2d":
+                    ds.x_flat[m].copy_(pinned[m], non_blocking=True)
+                else:
+                    head_out[m].copy_(ds.passes[m][-1][3], non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b), dist, device)
 
-    # ---- vocab-sharded lm_head + NCCL all-gather of the logits (N > 1)
+    copies("h2d")
+    t_h2d, t_d2h = copies("h2d"), copies("d2h")
+    host_link = {"h2d_ms_per_step": round(t_h2d, 4), "h2d_GB/s_per_rank": round(h2d / (t_h2d * 1e-3) / 1e9, 1),
+                 "d2h_ms_per_step": round(t_d2h, 4), "d2h_GB/s_per_rank": round(d2h / (t_d2h * 1e-3) / 1e9, 1),
+                 "copies_alone_ms": round(t_h2d + t_d2h, 4),
+                 "note": "the step's host copies alone, every rank at once; e2e cannot beat the larger of the "
+                         "copy time and the device time"}
+    del per_m_graph
+
+    head_alone = ds.head_alone(hbm, device)
     sharded = None
     if world > 1 or args.lm_head_shard:
-        full = passes[ms_list[0]][-1][1]
-        vocab = full.shape[0]
-        lo, hi = kl.sharded_head.shard_bounds(vocab, world, rank)
-        if fmt == "w4_asym":
-            shard = kl.PackedInt4Asym(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous(),
-                                      full.zeros[lo:hi].contiguous(), full.group_size)
-        else:
-            shard = kl.RowwiseInt8(full.data[lo:hi].contiguous(), full.scales[lo:hi].contiguous())
-        shead = kl.VocabShardedHead(shard, vocab)
-        sharded = {"vocab": vocab, "ranks": world, "rows_per_rank": hi - lo, "per_m": {}}
-        for m in ms_list:
-            x = passes[m][-1][2]
-            gathered = torch.empty(vocab, m, dtype=torch.bfloat16, device=device)
-            for _ in range(3):
-                shead(x, gathered=gathered)
-            barrier()
-            # shard GEMM + all-gather captured once and replayed (no host launch gaps);
-            # the graph is released before the process group is torn down
-            sg = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(sg):
-                shead(x, gathered=gathered)
-            sg.replay()
-            barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = max(5, args.steps)
-            a.record()
-            for _ in range(reps):
-                sg.replay()
-            b.record()
-            barrier()
-            del sg
-            t = a.elapsed_time(b) / reps
-            if dist is not None:
-                tt = torch.tensor([t], device=device)
-                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                t = tt.item()
-            # fused alternative: shard GEMM + local top-8 + gather of candidates + merge
-            for _ in range(3):
-                shead.topk(x, 8)
-            barrier()
-            tg = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(tg):
-                shead.topk(x, 8)
-            tg.replay()
-            barrier()
-            a.record()
-            for _ in range(reps):
-                tg.replay()
-            b.record()
-            barrier()
-            del tg
-            tk = a.elapsed_time(b) / reps
-            if dist is not None:
-                tt = torch.tensor([tk], device=device)
-                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                tk = tt.item()
-            sharded["per_m"][str(m)] = {"ms": round(t, 4), "allgather_bytes": vocab * m * 2,
-                                        "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1),
-                                        "top8_ms": round(tk, 4), "top8_gather_bytes": world * m * 8 * 8}
+        sharded = sharded_head_section(kl, ds.passes[ms_list[0]][-1][1], ms_list,
+                                       lambda m: ds.passes[m][-1][2], world, rank, device, dist, args.steps, fmt)
 
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     result = {
@@ -500,26 +547,186 @@ def bench_decode(args, kl, world, rank, local, dist):
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": workload_desc,
-                   "batch_m": ms_list, "gemms_per_pass": len(passes[ms_list[0]]),
+                   "batch_m": ms_list, "gemms_per_pass": len(ds.passes[ms_list[0]]), "passes_per_step": passes,
                    "bytes_per_step": step_bytes, "weights": ("4-bit asym, bf16 scale/zero per 128-group" if fmt == "w4_asym" else "int8 per-row bf16 scale")
                               + ", N(0,0.02) seeded",
-                   "l2": "inputs larger than L2: each pass streams >=0.6 GB of weights, no flush needed",
+                   "l2": "inputs larger than L2: each pass streams >=0.3 GB of weights, no flush needed",
                    "parallelism": f"replicas x{world}",
-                   "launch": "one grouped tcgen05 launch per M (113 independent GEMMs), CUDA graph"},
+                   "launch": "one grouped tcgen05 launch per M (all GEMMs of the pass, independent), "
+                             "passes_per_step passes per step in one CUDA graph"},
         "per_m": per_m,
-        "roofline": {"bound": "hbm", "kernel": "tc_qgemm_kernel (the step's 4 grouped launches)",
+        "roofline": {"bound": "hbm", "kernel": "tc_qgemm_kernel (the step's grouped launches)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
                      "traffic": profiled_traffic(f"{args.workload}_step"),
-                     "lm_head_alone": {"ms": round(head_ms, 4), "GB/s": round(head_gbs, 1),
-                                       "frac": round(head_gbs / hbm, 3), "m": m0}},
+                     "lm_head_alone": head_alone},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 4)},
+                "ms_per_step": round(e2e_ms, 4), "host_link": host_link},
         "lm_head_sharded": sharded,
-        "gpu_launches": len(ms_list) * args.steps,
+        "gpu_launches": passes * len(ms_list) * args.steps,
         "clocks": clocks.summary(),
     }
+    if args.workload == "decode" and not args.only_headline:
+        del ds
+        torch.cuda.empty_cache()
+        qwen_w8 = weights[:-1]
+        result["config0"] = section_config0(kl, device, hbm, dist)
+        result["prefill"] = section_prefill(kl, qwen_w8, device, tf_burst, peak_kind, args, rank, world, dist)
+        del weights, qwen_w8
+        torch.cuda.empty_cache()
+        result["w4"] = section_decode_other(kl, "w4", device, hbm, args, rank, world, dist)
+        result["llama"] = section_decode_other(kl, "llama", device, hbm, args, rank, world, dist)
     return result
+
+
+def section_config0(kl, device, hbm, dist):
+    """one gate_proj-shaped linear (x bf16 [1, 1024], W
+    [3072, 1024] ~ N(0, 0.02), per-row int8).  64 differently seeded copies of
+    the weights (200 MB, larger than L2) are cycled, each call a dependent launch
+    (programmatic dependent launch, one CUDA graph), on each kernel that takes
+    the shape."""
+    import torch
+    n, k, copies = 3072, 1024, 64
+    gen = torch.Generator(device=device)
+    ws = []
+    for i in range(copies):
+        gen.manual_seed(1000 + i)
+        ws.append(kl.quantize_int8_rowwise(torch.randn(n, k, device=device, generator=gen) * 0.02))
+    gen.manual_seed(0)
+    x = torch.randn(1, k, device=device, generator=gen).to(torch.bfloat16)
+    y = torch.empty(1, n, device=device, dtype=torch.bfloat16)
+    nbytes = n * k + 2 * n + 2 * k + 2 * n
+    out = {"shape": [1, n, k], "bytes_per_call": nbytes, "l2": f"{copies} weight copies cycled ({copies * n * k >> 20} MiB)"}
+    kernel_names = {None: "single-tile cluster tcgen05 (kl_tc_chain)", "persistent": "stream-K tcgen05 (tc_qgemm)",
+                    "simt": "CUDA-core GEMV (gemv_vec)"}
+    for path in (None, "persistent", "simt"):
+        def run(path=path):
+            for w in ws:
+                kl.quant_linear(x, w, out=y, pdl=True, path=path)
+        run()
+        torch.cuda.synchronize()
+        g = capture(run)
+        ms = max_over_ranks(timed(g, 10), dist, device) / copies
+        del g
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[path or "auto"] = {"us": round(ms * 1e3, 3), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
+                               "kernel": kernel_names[path]}
+    return out
+
+
+def section_prefill(kl, weights, device, tf_burst, peak_kind, args, rank, world, dist):
+    """the 28 layers' four GEMMs (the config 1 weights, 353 MB
+    of int8, larger than L2) at M in {512, 2048, 8192}, launched in model order
+    with programmatic dependent launch as one CUDA graph per M, without and with
+    the SwiGLU epilogue on gate_up.  TFLOP/s = 2*M*N*K summed / device time."""
+    import numpy as np
+    import torch
+    ms_list = [512, 2048, 8192]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(77 + rank)
+    res = {}
+    with ClockSampler(device.index or 0) as clocks:
+        for m in ms_list:
+            xs = {k: torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16) for k in (1024, 2048, 3072)}
+            row = {}
+            for sw in (False, True):
+                ys = {}
+                items = []
+                for name, p in weights:
+                    n, k = p.shape
+                    swn = sw and name.startswith("gate_up")
+                    key = (n // 2 if swn else n)
+                    if key not in ys:
+                        ys[key] = torch.empty(m, key, device=device, dtype=torch.bfloat16)
+                    items.append((p, xs[k], ys[key], swn))
+
+                def run(items=items):
+                    for p, x, y, swn in items:
+                        kl.quant_linear(x, p, out=y, swiglu=swn, pdl=True)
+                run()
+                torch.cuda.synchronize()
+                g = capture(run)
+                ms = max_over_ranks(timed(g, 3 if m == 8192 else 5), dist, device)
+                del g
+                flops = sum(2 * m * p.shape[0] * p.shape[1] for p, _, _, _ in items)
+                tfs = flops / (ms * 1e-3) / 1e12
+                row["swiglu" if sw else "plain"] = {"ms": round(ms, 3), "TFLOP/s": round(tfs, 1),
+                                                    "frac": round(tfs / tf_burst, 3)}
+            res[str(m)] = row
+            del xs
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the reference's CPU path (dequantise + fp32 matmul + bf16 cast) on a subset:
+        # M = 512 tokens against 1024-row slices of each of the four layer shapes
+        from oracle import quant_oracle as O
+        rng = np.random.default_rng(0)
+        t_total, flops = 0.0, 0
+        subset = [(1024, 1024), (1024, 2048), (1024, 1024), (1024, 3072)]
+        prepared = []
+        for n, k in subset:
+            q, sc = O.quantize_int8_rowwise(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+            prepared.append((q, sc, O.bf16_round(rng.standard_normal((512, k), dtype=np.float32))))
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 5.0:
+            for q, sc, x in prepared:
+                t1 = time.perf_counter()
+                O.linear(x, O.dequantize_int8_rowwise(q, sc))
+                t_total += time.perf_counter() - t1
+                flops += 2 * x.shape[0] * q.shape[0] * q.shape[1]
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+        cpu = {"value": round(flops / t_total / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"M=512 against 1024-row slices of the qkv/o/gate_up/down shapes ({t_total:.1f} s)"}
+    return {"unit": "TFLOP/s", "peak": tf_burst, "peak_source": peak_kind, "batch_m": ms_list,
+            "launch": "28 layers x 4 GEMMs per M in model order, programmatic dependent launch, one CUDA graph",
+            "per_m": res, "cpu_baseline": cpu, "clocks": clocks.summary()}
+
+
+def section_decode_other(kl, which, device, hbm, args, rank, world, dist):
+    """BASELINE config 3 (``w4``: 4-bit asymmetric group-128 weights, Qwen3-0.6B
+    decode shapes, M in {1, 16}) or config 4 (``llama``: Llama-3.2-3B shapes,
+    int8, M in {1, 64, 256}): the grouped launch and the dependent chain per M,
+    the lm_head alone, and at N > 1 the vocab-sharded lm_head."""
+    import torch
+    if which == "w4":
+        layer, head, ms_list, fmt = QWEN_LAYER, QWEN_HEAD, [1, 16], "w4_asym"
+    else:
+        layer, head, ms_list, fmt = LLAMA_LAYER, LLAMA_HEAD, [1, 64, 256], "w8_row"
+    weights = build_weights(kl, layer, LAYERS, device, seed=2024 if which == "w4" else 3030, fmt=fmt)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4322)
+    hw = torch.randn(head[1], head[2], device=device, generator=gen) * 0.02
+    weights.append(("lm_head", quantize(kl, hw, fmt)))
+    del hw
+    torch.cuda.empty_cache()
+    with ClockSampler(device.index or 0) as clocks:
+        ds = DecodeSet(kl, weights, ms_list, device, 199 + rank)
+        per_m = ds.per_m(hbm, 5, device, dist)
+        head_alone = ds.head_alone(hbm, device)
+    tf_burst = measured_peaks()[1]
+    for m in ms_list:
+        flops = sum(2 * m * p.shape[0] * p.shape[1] for _, p, _, _ in ds.passes[m])
+        for kind in ("grouped", "chain"):
+            t = per_m[str(m)][f"{kind}_ms"]
+            per_m[str(m)][f"{kind}_TFLOP/s"] = round(flops / (t * 1e-3) / 1e12, 1)
+            per_m[str(m)][f"{kind}_frac_tensor"] = round(flops / (t * 1e-3) / 1e12 / tf_burst, 3)
+            per_m[str(m)][f"{kind}_tokens/s_all_ranks"] = round(world * m / (t * 1e-3), 1)
+    out = {"workload": ("qwen3-0.6b decode projection set, 4-bit asym g128 (config 3)" if which == "w4"
+                        else "llama-3.2-3b projection set, int8 (config 4)"),
+           "batch_m": ms_list, "bytes_per_pass": {str(m): ds.pass_bytes(m) for m in ms_list},
+           "per_m": per_m, "lm_head_alone": head_alone, "clocks": clocks.summary()}
+    if world > 1:
+        out["lm_head_sharded"] = sharded_head_section(kl, ds.passes[ms_list[0]][-1][1], ms_list,
+                                                      lambda m: ds.passes[m][-1][2], world, rank, device, dist,
+                                                      args.steps, fmt)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        shapes = layer + [head]
+        v, secs, desc, threads = cpu_path_sample(shapes, [1], fmt, budget_s=5.0)
+        out["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                               "sample": desc + f" ({secs:.1f} s, M = 1 only)"}
+    del ds, weights
+    torch.cuda.empty_cache()
+    return out
 
 
 def bench_prefill(args, kl, world, rank, local, dist):
@@ -712,6 +919,7 @@ def main():
     ap.add_argument("--swiglu", action="store_true", help="prefill: fuse SwiGLU into gate_up")
     ap.add_argument("--lm-head-shard", action="store_true", help="llama: vocab-shard the lm_head + NCCL all-gather")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-headline", action="store_true", help="decode: skip the config 0/2/3/4 sections")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
