@@ -10,7 +10,7 @@ kernels in ``libkl_b200.so`` (C ABI: ``include/kl_b200.h``).
 The directory name contains hyphens, so import it with
 ``importlib.import_module("gpu-kernel-lab_b200")``.
 """
-from . import _native, kernel_policy, sharded_head
+from . import _native, kernel_policy, ops, sharded_head
 from .activation_int8 import (CalibratedInt8, RowwiseInt8, dequantize_int8, dequantize_int8_rowwise,
                               quantize_int8, quantize_int8_rowwise)
 from .cuda_decode import extension, project
@@ -33,5 +33,5 @@ __all__ = [
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
     "select_qwen_policy", "sharded_head", "VocabShardedHead",
     "export_packed", "save_packed", "load_packed", "install_packed", "packed_store",
-    "qwen_rmsnorm", "qwen_residual_rmsnorm", "rmsnorm",
+    "qwen_rmsnorm", "qwen_residual_rmsnorm", "rmsnorm", "ops",
 ]

@@ -122,30 +122,36 @@ def act_dtype_code(dtype: torch.dtype) -> int:
     raise ValueError(f"unsupported dtype {dtype}")
 
 
-# ---- per-device workspace --------------------------------------------------------
-# The tcgen05 kernel's split-K fixup needs scratch (arrival counters that must
-# start at zero, plus f32 partial tiles).  One zero-initialised buffer per
-# device is kept and grown on demand; the kernels leave the counters at zero.
-# Calls on different streams of one device that could overlap should pass their
-# own workspace (see ``linear.quant_linear(workspace=...)``).
-_workspaces: dict[int, torch.Tensor] = {}
+# ---- workspaces ---------------------------------------------------------------
+# The persistent tcgen05 kernel's split-K fixup needs scratch (arrival counters
+# that must start at zero, plus f32 partial tiles).  A zero-initialised buffer
+# is kept per device for the default stream and for CUDA-graph capture, and
+# one per (device, stream) for every other stream, so that calls on different
+# streams never share scratch; each grows on demand and the kernels leave the
+# counters at zero.  (Captured graphs replayed concurrently on different
+# streams should pass their own ``workspace``.)
+_workspaces: dict = {}
 _retired_workspaces: list = []
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+def workspace(device: torch.device, nbytes: int, stream=None) -> torch.Tensor | None:
     if nbytes == 0:
         return None
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    buf = _workspaces.get(idx)
+    capturing = torch.cuda.is_current_stream_capturing()
+    key = idx
+    if stream is not None and not capturing and stream != torch.cuda.default_stream(idx):
+        key = (idx, stream.cuda_stream)
+    buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
-        if torch.cuda.is_current_stream_capturing():
+        if capturing:
             raise RuntimeError("the first quantized-linear call on a device must happen before CUDA-graph "
                                "capture (it allocates the device workspace); run one warm-up call first")
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
-        if idx in _workspaces:
+        if key in _workspaces:
             # CUDA graphs captured earlier may still point at the old buffer: keep it alive
-            _retired_workspaces.append(_workspaces[idx])
-        _workspaces[idx] = buf
+            _retired_workspaces.append(_workspaces[key])
+        _workspaces[key] = buf
     return buf
 
 

@@ -14,6 +14,7 @@ from __future__ import annotations
 import torch
 
 from . import _native as N
+from . import ops as _ops  # noqa: F401  (registers torch.ops.kl_b200)
 from .activation_int8 import RowwiseInt8
 from .linear import quant_linear
 
@@ -41,25 +42,16 @@ def project(x, weight, *, warps=4, persistent=False, swiglu=False):
     if isinstance(weight, RowwiseInt8):
         return quant_linear(x, weight, swiglu=swiglu)
     n, k = w.shape
-    y = torch.empty(n // 2 if swiglu else n, dtype=torch.bfloat16, device=x.device)
-    lib = N.lib()
-    with torch.cuda.device(x.device):
-        if isinstance(weight, torch.Tensor):
-            if w.dtype != torch.bfloat16:
-                raise RuntimeError("BF16 or INT8 weights required")
-            status = lib.kl_project(N.ptr(x), k, N.ptr(w), 0, None, None, n, 128, warps, int(persistent),
-                                    int(swiglu), N.ptr(y), None, 0, N.stream_handle(x.device))
-        else:
-            if weight.scales.dtype != torch.float32 or weight.inverse.dtype != torch.float32 or \
-                    not weight.scales.is_contiguous() or not weight.inverse.is_contiguous():
-                raise RuntimeError("FP32 contiguous scaling buffers required")
-            if weight.scales.device != x.device or weight.inverse.device != x.device:
-                raise RuntimeError("scales must share device")
-            g = int(weight.group_size)
-            if g <= 0 or k % g or weight.scales.shape != (n, k // g) or weight.inverse.shape != (k,):
-                raise RuntimeError("scaling shapes incorrect")
-            status = lib.kl_project(N.ptr(x), k, N.ptr(w), 1, N.ptr(weight.scales), N.ptr(weight.inverse), n, g,
-                                    warps, int(persistent), int(swiglu), N.ptr(y), None, 0,
-                                    N.stream_handle(x.device))
-    N.check(status)
-    return y
+    if isinstance(weight, torch.Tensor):
+        if w.dtype != torch.bfloat16:
+            raise RuntimeError("BF16 or INT8 weights required")
+        return torch.ops.kl_b200.project(x, w, None, None, 128, warps, bool(persistent), bool(swiglu))
+    if weight.scales.dtype != torch.float32 or weight.inverse.dtype != torch.float32 or \
+            not weight.scales.is_contiguous() or not weight.inverse.is_contiguous():
+        raise RuntimeError("FP32 contiguous scaling buffers required")
+    if weight.scales.device != x.device or weight.inverse.device != x.device:
+        raise RuntimeError("scales must share device")
+    g = int(weight.group_size)
+    if g <= 0 or k % g or weight.scales.shape != (n, k // g) or weight.inverse.shape != (k,):
+        raise RuntimeError("scaling shapes incorrect")
+    return torch.ops.kl_b200.project(x, w, weight.scales, weight.inverse, g, warps, bool(persistent), bool(swiglu))

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _native as N
+from . import ops as _ops  # noqa: F401  (registers torch.ops.kl_b200)
 from .quantization import PackedInt4
 
 
@@ -30,13 +30,7 @@ def _validate(x, packed, block_n):
 
 def int4_gemv(x, packed: PackedInt4, block_n=32):
     _validate(x, packed, block_n)
-    n, k = packed.shape
-    output = torch.empty(n, device=x.device, dtype=x.dtype)
-    with torch.cuda.device(x.device):
-        N.check(N.lib().kl_int4_gemv(N.ptr(x), N.act_dtype_code(x.dtype), k, N.ptr(packed.data),
-                                     N.ptr(packed.scales), n, packed.group_size, block_n, N.ptr(output),
-                                     N.stream_handle(x.device)), ValueError)
-    return output
+    return torch.ops.kl_b200.int4_gemv(x, packed.data, packed.scales, packed.group_size, block_n)
 
 
 def int4_lm_head_topk(x, packed: PackedInt4, top_k=1, block_n=32):
@@ -49,14 +43,4 @@ def int4_lm_head_topk(x, packed: PackedInt4, top_k=1, block_n=32):
     n, k = packed.shape
     if not 1 <= top_k <= min(8, block_n, n):
         raise ValueError('top_k must be between 1 and min(8,block_n,vocabulary)')
-    lib = N.lib()
-    values = torch.empty(top_k, device=x.device, dtype=torch.float32)
-    ids = torch.empty(top_k, device=x.device, dtype=torch.int64)
-    need = lib.kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n)
-    ws = torch.empty(need, dtype=torch.uint8, device=x.device)
-    with torch.cuda.device(x.device):
-        N.check(lib.kl_int4_lm_head_topk(N.ptr(x), N.act_dtype_code(x.dtype), k, N.ptr(packed.data),
-                                         N.ptr(packed.scales), n, packed.group_size, top_k, block_n,
-                                         N.ptr(values), N.ptr(ids), N.ptr(ws), need,
-                                         N.stream_handle(x.device)), ValueError)
-    return values, ids
+    return torch.ops.kl_b200.int4_lm_head_topk(x, packed.data, packed.scales, packed.group_size, top_k, block_n)

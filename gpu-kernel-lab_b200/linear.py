@@ -21,6 +21,7 @@ import torch
 from torch import nn
 
 from . import _native as N
+from . import ops as _ops  # noqa: F401  (registers torch.ops.kl_b200)
 from .activation_int8 import CalibratedInt8, RowwiseInt8, quantize_int8_rowwise
 from .quantization import PackedInt4, PackedInt4Asym, quantize_int4, quantize_int4_asym
 
@@ -59,6 +60,9 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
     int8 linear that the single-tile cluster kernel would take).
     ``pdl``: launch with programmatic dependent launch (use inside a chain of
     launches / a CUDA graph to overlap weight prefetch with the previous kernel).
+    The launch goes through the registered operator ``torch.ops.kl_b200.linear``
+    (``linear_out`` when ``out`` is given).  ``workspace``: a caller-owned
+    scratch buffer; by default each (device, stream) pair has its own.
     """
     fmt, data, scales, zeros, inverse, n, k, group = weight_spec(weight)
     if torch.is_grad_enabled() and x.requires_grad:
@@ -78,13 +82,7 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
         x2 = x2.contiguous()
     n_out = n // 2 if swiglu else n
     shape = (n_out, m) if transposed else (*lead, n_out)
-    if out is None:
-        out = torch.empty(shape, dtype=x.dtype, device=x.device)
-    elif tuple(out.shape) != tuple(shape) or out.dtype != x.dtype or not out.is_contiguous():
-        raise RuntimeError("out has the wrong shape, dtype or layout")
-    if m == 0:
-        return out
-    flags = (N.KL_FLAG_PDL if pdl else 0) | (N.KL_FLAG_Y_TRANSPOSED if transposed else 0)
+    flags = N.KL_FLAG_PDL if pdl else 0
     if path == "tc":
         flags |= N.KL_FLAG_FORCE_TC
     elif path == "simt":
@@ -93,18 +91,14 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
         flags |= N.KL_FLAG_FORCE_TC | N.KL_FLAG_PERSISTENT
     elif path is not None:
         raise ValueError(f"unknown path {path!r}")
-    lib = N.lib()
-    with torch.cuda.device(x.device):
-        if workspace is None:
-            need = lib.kl_linear_workspace_bytes(m, n, k, fmt, int(swiglu), flags)
-            ws = N.workspace(x.device, need)
-        else:
-            ws = workspace
-        N.check(lib.kl_linear(
-            N.ptr(x2), N.act_dtype_code(x.dtype), m, k, N.ptr(data), fmt, n, group,
-            N.ptr(scales), N.ptr(zeros), N.ptr(inverse), int(swiglu), N.ptr(out),
-            N.ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(), flags,
-            N.stream_handle(x.device)))
+    if out is None:
+        y = torch.ops.kl_b200.linear(x2, data, scales, zeros, inverse, fmt, group, swiglu, transposed, flags,
+                                     workspace)
+        return y.view(shape)
+    if tuple(out.shape) != tuple(shape) or out.dtype != x.dtype or not out.is_contiguous():
+        raise RuntimeError("out has the wrong shape, dtype or layout")
+    torch.ops.kl_b200.linear_out(x2, data, scales, zeros, inverse, fmt, group, swiglu, transposed, flags,
+                                 out.view(shape if transposed else (m, n_out)), workspace)
     return out
 
 
