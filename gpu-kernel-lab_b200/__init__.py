@@ -19,7 +19,8 @@ from .linear import GroupedLinear, QuantLinear, quant_linear, weight_spec
 from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequantize_int4_asym, quantize_int4,
                            quantize_int4_asym)
 from .native_ops import dequantize_native
-from .adapters import install_quantized_projections
+from .adapters import install_quantized_executor, install_quantized_projections
+from .quant_tensor import QuantWeight
 from .packed_store import export_packed, install_packed, load_packed, save_packed
 from .rmsnorm import qwen_residual_rmsnorm, qwen_rmsnorm
 from .sharded_head import VocabShardedHead
@@ -33,5 +34,5 @@ __all__ = [
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
     "select_qwen_policy", "sharded_head", "VocabShardedHead",
     "export_packed", "save_packed", "load_packed", "install_packed", "packed_store",
-    "qwen_rmsnorm", "qwen_residual_rmsnorm", "rmsnorm", "ops",
+    "qwen_rmsnorm", "qwen_residual_rmsnorm", "rmsnorm", "ops", "QuantWeight", "install_quantized_executor",
 ]

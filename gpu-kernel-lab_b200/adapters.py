@@ -11,6 +11,14 @@ Restates the module patches of the reference's
 * gate and up run as ONE launch with the SwiGLU epilogue fused
   (``mlp.forward`` becomes ``down(silu(gate) * up)``).
 * o_proj, down_proj and (optionally) lm_head become :class:`QuantLinear`.
+* Every replaced module keeps a ``weight`` attribute: a :class:`QuantWeight`
+  (no dense values) over its rows of the packed matrix.  ``torch.cat`` of the
+  Q/K/V (or gate/up) weights gives back the fused packed matrix without a copy
+  and ``F.linear`` on it runs the quantized kernel, so the reference's serving
+  executor (``serving/qwen_executor.py:90-108`` builds its fused weights that
+  way; ``:171-174,227-237`` call them) runs on the quantized kernels unchanged;
+  :func:`install_quantized_executor` covers an executor built before the
+  install.
 
 Unlike the reference adapter, every batch size runs on the quantized kernels
 (decode M <= 64 on the HBM-bound path, prefill on the tensor-core path), and
@@ -25,6 +33,7 @@ import torch
 from torch import nn
 
 from .linear import QuantLinear, quant_linear
+from .quant_tensor import QuantWeight
 
 FORMATS = ("w8_row", "w4_asym", "w4_sym")
 
@@ -35,6 +44,7 @@ class _FusedQKV:
     def __init__(self, weight: QuantLinear, sizes):
         self.weight = weight
         self.sizes = tuple(int(s) for s in sizes)
+        self.offsets = [sum(self.sizes[:i]) for i in range(len(self.sizes) + 1)]
         self.pending: dict[int, torch.Tensor] = {}
 
     def reset(self, module, args):
@@ -51,6 +61,12 @@ class QKVSlice(nn.Module):
         self.in_features = in_features
         self.out_features = fused.sizes[slot]
 
+    @property
+    def weight(self) -> QuantWeight:
+        """This projection's rows of the fused packed matrix (no dense values)."""
+        f = self.fused
+        return f.weight.weight.slice_rows(f.offsets[self.slot], f.offsets[self.slot + 1])
+
     def forward(self, x):
         f = self.fused
         if self.slot == 0:
@@ -63,6 +79,29 @@ class QKVSlice(nn.Module):
 
     def extra_repr(self):
         return f"slot={self.slot}, out_features={self.out_features}, fused={self.fused.weight.format}"
+
+
+class RowSlice(nn.Module):
+    """gate_proj or up_proj after the install: rows ``[lo, hi)`` of the fused
+    gate_up matrix.  The MLP's forward runs the fused launch; this module keeps
+    the attribute (and a direct call computes just its rows)."""
+
+    def __init__(self, fused: QuantLinear, lo: int, hi: int):
+        super().__init__()
+        self.fused = fused
+        self.lo, self.hi = lo, hi
+        self.in_features = fused.in_features
+        self.out_features = hi - lo
+
+    @property
+    def weight(self) -> QuantWeight:
+        return self.fused.weight.slice_rows(self.lo, self.hi)
+
+    def forward(self, x):
+        return quant_linear(x, self.weight.packed)
+
+    def extra_repr(self):
+        return f"rows=[{self.lo}, {self.hi}), fused={self.fused.format}"
 
 
 def _check_bias_free(*modules):
@@ -163,7 +202,9 @@ def _install(model, plan: dict, head_fmt, make) -> dict:
             attn.v_proj = QKVSlice(fused, 2, in_features)
             attn.o_proj = o_q
             mlp.kl_gate_up = gate_up
-            del mlp.gate_proj, mlp.up_proj
+            half = gate.out_features
+            mlp.gate_proj = RowSlice(gate_up, 0, half)
+            mlp.up_proj = RowSlice(gate_up, half, 2 * half)
             mlp.down_proj = down_q
             mlp.forward = types.MethodType(_mlp_forward, mlp)
             replaced += 7
@@ -183,4 +224,18 @@ def _install(model, plan: dict, head_fmt, make) -> dict:
             "layout": "fused QKV (one launch), fused gate_up + SwiGLU (one launch), o, down"
                       + (", lm_head" if head_fmt else "")}
     model._kl_b200_info = info
+    return info
+
+
+def install_quantized_executor(executor, policy=None, **kwargs) -> dict:
+    """Quantize the projections of a serving executor's model (the reference's
+    ``QwenPagedExecutor``: anything with ``.model`` and, optionally,
+    ``enable_fused_projections`` / ``fused_qkv_layers`` / ``fused_mlp_layers``)
+    and rebuild fused weights it already prepacked, so that its fused QKV and
+    gate_up ``F.linear`` sites run the quantized kernel too.  ``policy`` and
+    ``kwargs`` are those of :func:`install_quantized_projections`."""
+    info = install_quantized_projections(executor.model, policy, **kwargs)
+    if getattr(executor, "_projection_weights", None) is not None:
+        executor.enable_fused_projections(qkv=executor.fused_qkv_layers, mlp=executor.fused_mlp_layers)
+        info["executor_fused_weights"] = "rebuilt from the quantized modules"
     return info

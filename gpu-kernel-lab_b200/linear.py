@@ -140,6 +140,17 @@ class QuantLinear(nn.Module):
             raise ValueError("bias-free projections required")
         return cls.from_weight(linear.weight, fmt, group_size)
 
+    @property
+    def weight(self):
+        """The packed matrix as a :class:`~.quant_tensor.QuantWeight` (``F.linear``
+        and ``torch.cat`` work on it; it has no dense values)."""
+        from .quant_tensor import QuantWeight
+        qw = self.__dict__.get("_qweight")
+        if qw is None or qw.packed is not self.weight_q:
+            qw = QuantWeight(self.weight_q)
+            self.__dict__["_qweight"] = qw
+        return qw
+
     def forward(self, x):
         return quant_linear(x, self.weight_q, swiglu=self.swiglu)
 

@@ -35,7 +35,8 @@ def test_install_structure_on_cpu():
     assert isinstance(attn0.q_proj, torch.nn.Linear)                      # layer 0 untouched
     assert isinstance(attn1.q_proj, kl.adapters.QKVSlice) and attn1.q_proj.out_features == 256
     assert attn1.k_proj.out_features == 128 and attn1.v_proj.out_features == 128
-    assert not hasattr(model.model.layers[1].mlp, "gate_proj")             # dense gate/up released
+    gp = model.model.layers[1].mlp.gate_proj                              # dense gate/up released
+    assert isinstance(gp, kl.adapters.RowSlice) and isinstance(gp.weight, kl.QuantWeight)
     assert isinstance(model.lm_head, kl.QuantLinear)
     assert info["packed_bytes"] < info["dense_bytes_released"]
     # the reference's call-order rule: k before q is an error (no kernel is reached)

@@ -47,7 +47,11 @@ def test_install_on_meta_model_reads_no_dense_weight(tmp_path):
     info = kl.install_packed(dst, kl.load_packed(path))
     assert info["dense_bytes_released"] == 0 and info["packed_bytes"] == src._kl_b200_info["packed_bytes"]
     assert dst.model.layers[1].self_attn.kl_qkv.weight_q.data.device.type == "cpu"
-    assert not hasattr(dst.model.layers[0].mlp, "gate_proj")
+    # gate_proj / up_proj are row views of the packed gate_up matrix: no dense (meta) weight is left
+    gp = dst.model.layers[0].mlp.gate_proj
+    assert isinstance(gp, kl.adapters.RowSlice) and gp.weight.packed.data.device.type == "cpu"
+    assert not any(p.device.type == "meta" for n, p in dst.named_parameters()
+                   if ".layers." in n and ("_proj" in n))
 
 
 def test_shape_and_plan_mismatches_raise(tmp_path):
