@@ -198,6 +198,7 @@ def run_reference(args):
             if i >= args.warmup:
                 vals.append(v)
     value = statistics.mean(vals)
+    gpu_context = reference_gpu_context(args)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per_step * 1000, 1), "higher_is_better": True, "scaling": "weak",
@@ -206,8 +207,85 @@ def run_reference(args):
                        "path": "reference CPU path (dequantise + fp32 matmul + bf16 cast), bounded row samples"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc + f" ({per_step:.1f} s per step)"},
-            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_context": gpu_context}
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_context(args):
+    """GPU context, not part of the CPU arm's value: the reference's own CUDA
+    decode op (``learning/10_cuda_decode/warp_gemv.cu``, built unmodified by
+    ``oracle/build_ref.py``) on this GPU, at config 0 and over the config 1
+    projection set at M = 1 (its only batch size), launched one by one in model
+    order and captured in a CUDA graph.  Weights are per-row int8 made with
+    plain torch (scale = absmax/127 as f32 [N, 1], inverse of ones: the
+    reference's calibrated format with group = K)."""
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+        from oracle import build_ref
+        mod = build_ref.load()
+    except Exception as e:            # noqa: BLE001 -- context only, never fatal
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    if mod is None:
+        return {"unavailable": "the reference extension was not built (oracle/build_ref.py)"}
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device)
+
+    def quant(n, k, seed):
+        gen.manual_seed(seed)
+        w = torch.randn(n, k, device=device, generator=gen) * 0.02
+        s = w.abs().amax(1, keepdim=True) / 127
+        s = torch.where(s == 0, torch.ones_like(s), s)
+        q = torch.round(w / s).clamp(-127, 127).to(torch.int8)
+        return q, s.float().contiguous()
+
+    def graph_ms(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(3):
+            g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    out = {"kernel": "reference warp_gemv.cu projection<QUANT> (unmodified, sm_100, warps=4)"}
+    # config 0: 64 weight copies cycled (larger than L2)
+    k = 1024
+    ones = torch.ones(k, device=device)
+    ws = [quant(3072, k, 1000 + i) for i in range(64)]
+    gen.manual_seed(0)
+    x = torch.randn(k, device=device, generator=gen).to(torch.bfloat16)
+    ms = graph_ms(lambda: [mod.project(x, q, s, ones, k, 4, False, False) for q, s in ws], 10) / 64
+    nbytes = 3072 * k + 2 * 3072 + 2 * k + 2 * 3072
+    out["config0"] = {"us": round(ms * 1e3, 3), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+    del ws
+    # config 1 at M = 1: 28 layers + lm_head in model order
+    items = []
+    for li in range(LAYERS):
+        for j, (name, n, kk) in enumerate(QWEN_LAYER):
+            q, s = quant(n, kk, 1234 + li * 16 + j)
+            items.append((q, s, torch.ones(kk, device=device), kk, name == "gate_up",
+                          torch.randn(kk, device=device, generator=gen).to(torch.bfloat16)))
+    q, s = quant(QWEN_HEAD[1], QWEN_HEAD[2], 4321)
+    items.append((q, s, torch.ones(QWEN_HEAD[2], device=device), QWEN_HEAD[2], False,
+                  torch.randn(QWEN_HEAD[2], device=device, generator=gen).to(torch.bfloat16)))
+    ms = graph_ms(lambda: [mod.project(xx, qq, ss, inv, kk, 4, False, sw) for qq, ss, inv, kk, sw, xx in items], 5)
+    nbytes = sum(qq.numel() + 2 * qq.shape[0] + 2 * kk + 2 * (qq.shape[0] // 2 if sw else qq.shape[0])
+                 for qq, ss, inv, kk, sw, xx in items)
+    out["config1_m1_chain"] = {"ms": round(ms, 4), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                               "gemms": len(items),
+                               "bytes_note": "the per-row format's bytes (int8 weights + bf16 scales + x + y), "
+                                             "the same count as the headline's"}
+    return out
 
 
 METRIC = "W8A16 GEMM HBM GB/s (decode M<=64) and TFLOP/s (prefill), Qwen3-0.6B shapes"

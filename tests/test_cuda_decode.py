@@ -99,3 +99,17 @@ def test_project_rowwise_format(swiglu):
     if swiglu:
         ref = O.swiglu(O.bf16_round(ref))
     assert_matches_oracle(y, ref, what="rowwise project")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["cal_a", "cal_a_rtn", "cal_b", "cal_b_g64"])
+def test_calibrated_dequantize_on_gpu_matches_reference_bits(golden, case):
+    """kl_dequantize(KL_W8_GROUP) reproduces the reference's dequantize_int8
+    (activation_int8.py:63-64, f32 q * s * inverse in that order) bit for bit
+    on the weights the reference itself calibrated."""
+    w = kl.CalibratedInt8(torch.from_numpy(golden[f"{case}_data"]).cuda(),
+                          torch.from_numpy(golden[f"{case}_scales"]).cuda(),
+                          torch.from_numpy(golden[f"{case}_inverse"]).cuda(),
+                          int(golden[f"{case}_group"]), float(golden[f"{case}_alpha"]), float(golden[f"{case}_mse"]))
+    got = kl.dequantize_native(w).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), golden[f"{case}_deq"].view(np.uint32))
