@@ -427,13 +427,22 @@ class DecodeSet:
 
     def head_alone(self, hbm, device):
         """The largest single GEMM (the lm_head) at the first batch size, graph-timed."""
+        import torch
         name, p, x, y = self.passes[self.ms_list[0]][-1]
         g = capture(lambda: [self.kl.quant_linear(x, p, out=y, pdl=True) for _ in range(5)])
         ms = timed(g, 4) / 5
+        del g
         m0 = self.ms_list[0]
         n, k = p.shape
         gbs = (p.storage_bytes + 2 * m0 * k + 2 * m0 * n) / (ms * 1e-3) / 1e9
-        return {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "m": m0}
+        out = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "m": m0}
+        # the same head with the top-8 selected in the GEMM's epilogue (no logits written)
+        self.kl.lm_head_topk(x, p, 8)
+        torch.cuda.synchronize()
+        g = capture(lambda: [self.kl.lm_head_topk(x, p, 8) for _ in range(5)])
+        out["top8_fused_ms"] = round(timed(g, 4) / 5, 4)
+        del g
+        return out
 
 
 def sharded_head_section(kl, full, ms_list, x_of, world, rank, device, dist, steps, fmt="w8_row"):

@@ -15,7 +15,7 @@ from .activation_int8 import (CalibratedInt8, RowwiseInt8, dequantize_int8, dequ
                               quantize_int8, quantize_int8_rowwise)
 from .cuda_decode import extension, project
 from .kernels import int4_gemv, int4_lm_head_topk
-from .linear import GroupedLinear, QuantLinear, quant_linear, weight_spec
+from .linear import GroupedLinear, QuantLinear, lm_head_topk, quant_linear, weight_spec
 from .quantization import (PackedInt4, PackedInt4Asym, dequantize_int4, dequantize_int4_asym, quantize_int4,
                            quantize_int4_asym)
 from .native_ops import dequantize_native
@@ -30,7 +30,7 @@ __all__ = [
     "CalibratedInt8", "RowwiseInt8", "PackedInt4", "PackedInt4Asym", "QuantLinear",
     "quantize_int8", "dequantize_int8", "quantize_int8_rowwise", "dequantize_int8_rowwise",
     "quantize_int4", "dequantize_int4", "quantize_int4_asym", "dequantize_int4_asym",
-    "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "weight_spec", "GroupedLinear",
+    "project", "extension", "int4_gemv", "int4_lm_head_topk", "quant_linear", "lm_head_topk", "weight_spec", "GroupedLinear",
     "dequantize_native", "install_quantized_projections", "kernel_policy", "QwenKernelPolicy", "load_qwen_policy",
     "select_qwen_policy", "sharded_head", "VocabShardedHead",
     "export_packed", "save_packed", "load_packed", "install_packed", "packed_store",

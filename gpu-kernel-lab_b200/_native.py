@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "kl_device_status", "kl_version", "kl_describe_plan",
     "kl_grouped_table_bytes", "kl_grouped_encode", "kl_grouped_workspace_bytes", "kl_linear_grouped",
     "kl_linear_noalloc", "kl_topk_rows_workspace_bytes", "kl_topk_rows", "kl_topk_merge_rows", "kl_rmsnorm",
+    "kl_linear_topk", "kl_linear_topk_workspace_bytes",
 )
 
 
@@ -62,6 +63,8 @@ _SIGNATURES = {
     "kl_topk_rows": (_I, [_P, _I, _I, _I, ctypes.c_longlong, ctypes.c_longlong, _I, _P, _P, _P, _S, _P]),
     "kl_topk_merge_rows": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "kl_rmsnorm": (_I, [_P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P]),
+    "kl_linear_topk": (_I, [_P, _I, _I, _I, _P, _I, _I, _I, _P, _P, _I, ctypes.c_longlong, _P, _P, _P, _S, _I, _P]),
+    "kl_linear_topk_workspace_bytes": (_S, [_I, _I, _I, _I, _I]),
 }
 
 _lib = None

@@ -205,6 +205,8 @@ using namespace kl;
 
 extern "C" {
 
+size_t kl_linear_topk_workspace_bytes(int m, int n, int k, int w_format, int top_k);
+
 const char* kl_status_string(int status) {
   switch (status) {
     case KL_OK: return "ok";
@@ -345,7 +347,8 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
       p.counters = static_cast<int*>(workspace);
       p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
       p.status = di.status;
-      const cudaError_t e = launch_tc(p, plan, w_format, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
+      const cudaError_t e = launch_tc(p, plan, w_format, swiglu ? kEpiSwiglu : kEpiPlain, xbf16,
+                                      (flags & KL_FLAG_PDL) != 0, s);
       if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
     }
     return KL_OK;
@@ -487,7 +490,7 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   p.status = di.status;
-  const cudaError_t e = launch_tc(p, plan, hd->w_format, hd->swiglu != 0, hd->x_dtype == KL_DT_BF16,
+  const cudaError_t e = launch_tc(p, plan, hd->w_format, hd->swiglu ? kEpiSwiglu : kEpiPlain, hd->x_dtype == KL_DT_BF16,
                                   (flags & KL_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "grouped tcgen05 GEMM launch");
   return KL_OK;
@@ -519,12 +522,21 @@ int kl_int4_gemv(const void* x, int x_dtype, int k, const uint8_t* w, const floa
                    KL_FLAG_FORCE_SIMT, stream);
 }
 
+// Workspace of kl_int4_lm_head_topk: the fused path's (stream-K counters, which
+// must stay zero between calls, partials and candidates), or for the other
+// shapes the logits and candidates placed after the counter area.
 size_t kl_int4_lm_head_topk_workspace_bytes(int n, int top_k, int block_n) {
   (void)block_n;
   if (n <= 0 || top_k <= 0) return 0;
   const size_t logits = (static_cast<size_t>(n) * 2 + 255) & ~size_t(255);
-  return logits + head_topk_candidate_bytes(n, top_k);
+  return kCounterBytes + logits + head_topk_candidate_bytes(n, top_k);
 }
+namespace {
+size_t int4_head_fused_bytes(int n, int k, int group, int top_k) {
+  if (group != 128 || k % 128 != 0) return 0;
+  return kl_linear_topk_workspace_bytes(1, n, k, KL_W4_SYM, top_k);
+}
+}  // namespace
 
 int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w, const float* scales, int n, int group,
                          int top_k, int block_n, float* values, int64_t* ids, void* workspace, size_t workspace_bytes,
@@ -532,9 +544,16 @@ int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w, co
   if (!values || !ids) return fail(KL_ERR_INVALID, "values and ids must be non-null");
   if (top_k < 1 || top_k > 8 || top_k > block_n || top_k > n)
     return fail(KL_ERR_INVALID, "top_k must be between 1 and min(8,block_n,vocabulary)");
+  // bf16, groups of 128: the tcgen05 GEMM selects candidates in its epilogue and
+  // the logits are never written (the reference's _head_candidates,
+  // learning/09_int4/kernels.py:37-50)
+  const size_t fused = x_dtype == KL_DT_BF16 ? int4_head_fused_bytes(n, k, group, top_k) : 0;
+  if (fused && workspace && workspace_bytes >= fused && aligned16(x) && aligned16(w))
+    return kl_linear_topk(x, x_dtype, 1, k, w, KL_W4_SYM, n, group, scales, nullptr, top_k, 0, values, ids,
+                          workspace, workspace_bytes, 0, stream);
   const size_t need = kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n);
   if (!workspace || workspace_bytes < need) return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required", need);
-  char* logits = static_cast<char*>(workspace);
+  char* logits = static_cast<char*>(workspace) + kCounterBytes;
   char* cand = logits + ((static_cast<size_t>(n) * 2 + 255) & ~size_t(255));
   int rc = kl_int4_gemv(x, x_dtype, k, w, scales, n, group, block_n, logits, stream);
   if (rc != KL_OK) return rc;
@@ -561,6 +580,106 @@ int kl_topk_rows(const void* logits, int dtype, int rows, int n, long long ld, l
   const cudaError_t e = launch_topk_rows(logits, dtype == KL_DT_BF16, rows, n, ld, index_offset, top_k, workspace,
                                          values, ids, static_cast<cudaStream_t>(stream), values == nullptr);
   return e == cudaSuccess ? KL_OK : cuda_fail(e, "top-k launch");
+}
+
+namespace {
+// Plan of the fused lm_head top-k: the persistent tcgen05 kernel with the top-k
+// epilogue (4-bit formats: at most 64 tokens per launch).
+struct TopkPlan {
+  bool ok;
+  int n_mma, kblk;
+  TcPlan tc;
+  long long units;
+  int n_tiles;
+  size_t cand_offset, bytes;
+};
+TopkPlan plan_topk(int m, int n, int k, int w_format, int top_k, int sm_count, const void* zeros) {
+  TopkPlan t{};
+  t.ok = false;
+  if (m <= 0 || n <= 0 || k <= 0 || top_k < 1 || top_k > 8) return t;
+  if (!(w_format == KL_W8_ROW || (is_w4(w_format) && m <= 64))) return t;
+  if (!tc_shape_ok(k, w_format, is_w4(w_format) ? 128 : k)) return t;
+  t.n_mma = tc_choose_nmma(m, w_format);
+  t.kblk = choose_kblk_single(m, n, k, w_format, t.n_mma, false, sm_count, zeros);
+  t.units = problem_units(m, n, k, t.n_mma, t.kblk, false);
+  t.tc = plan_tc(t.n_mma, t.kblk, t.units, w_format, sm_count);
+  if (!t.tc.ok) return t;
+  t.n_tiles = (n + 127) / 128;
+  t.cand_offset = (t.tc.workspace + 255) & ~size_t(255);
+  t.bytes = t.cand_offset + static_cast<size_t>(m) * t.n_tiles * top_k * sizeof(long long);
+  t.ok = true;
+  return t;
+}
+int sm_count_or_default() {
+  int sm = 148, dev = 0, v = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+    sm = v;
+  else
+    cudaGetLastError();
+  return sm;
+}
+}  // namespace
+
+size_t kl_linear_topk_workspace_bytes(int m, int n, int k, int w_format, int top_k) {
+  // the zeros pointer is not known here: size for whichever K block the call picks
+  const int sm = sm_count_or_default();
+  const TopkPlan a = plan_topk(m, n, k, w_format, top_k, sm, nullptr);
+  if (!a.ok) return 0;
+  size_t need = a.bytes;
+  if (w_format == KL_W4_ASYM) {     // a 16-byte-aligned zeros pointer may take the two-group stages
+    alignas(16) static const char probe[16] = {};
+    const TopkPlan b = plan_topk(m, n, k, w_format, top_k, sm, probe);
+    if (b.ok && b.bytes > need) need = b.bytes;
+  }
+  return need;
+}
+
+int kl_linear_topk(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
+                   const void* scales, const void* zeros, int top_k, long long index_offset, float* values,
+                   int64_t* ids, void* workspace, size_t workspace_bytes, int flags, void* stream) {
+  int rc = validate_linear(x, x_dtype, m, k, w, w_format, n, is_grouped(w_format) ? group : k, scales, zeros,
+                           nullptr, 0, ids, 0);
+  if (rc != KL_OK) return rc;
+  if (top_k < 1 || top_k > 8 || top_k > n) return fail(KL_ERR_INVALID, "top_k must be in [1, min(8, N)]");
+  if (index_offset < 0 || index_offset + n > 0x7FFFFFFFll) return fail(KL_ERR_INVALID, "row ids must stay below 2^31");
+  DeviceInfo di;
+  if ((rc = device_info(&di)) != KL_OK) return rc;
+  if (!(di.major == 10 && di.minor == 0))
+    return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
+  if (x_dtype != KL_DT_BF16 || !aligned16(x) || !aligned16(w) || (is_w4(w_format) && group != 128))
+    return fail(KL_ERR_UNSUPPORTED, "the fused top-k takes bf16 activations, 16-byte-aligned operands and, for "
+                                    "4-bit weights, groups of 128");
+  const TopkPlan tp = plan_topk(m, n, k, w_format, top_k, di.sm_count, zeros);
+  if (!tp.ok) return fail(KL_ERR_UNSUPPORTED, "no fused top-k plan for m=%d n=%d k=%d format %d", m, n, k, w_format);
+  if (!workspace || workspace_bytes < tp.bytes)
+    return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", tp.bytes,
+                workspace ? workspace_bytes : 0);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(ws + tp.cand_offset);
+  TcParams p;
+  std::memset(&p, 0, sizeof(p));
+  // y is never written in this epilogue; the candidate buffer stands in for it
+  rc = build_problem(p.single, x, x_dtype, m, k, w, w_format, n, scales, zeros, 0, cand, false, n, tp.n_mma, tp.kblk);
+  if (rc != KL_OK) return rc;
+  p.single.unit_begin = 0;
+  p.single.cand = cand;
+  p.single.topk = top_k;
+  p.single.cand_ld = tp.n_tiles * top_k;
+  p.single.index_offset = index_offset;
+  p.single.vec_store = 0;
+  p.count = 1;
+  p.w_stages = tp.tc.w_stages;
+  p.x_stages = tp.tc.x_stages;
+  p.units = tp.units;
+  p.counters = reinterpret_cast<int*>(ws);
+  p.partials = reinterpret_cast<float*>(ws + kCounterBytes);
+  p.status = di.status;
+  cudaError_t e = launch_tc(p, tp.tc, w_format, kEpiTopk, true, (flags & KL_FLAG_PDL) != 0, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch (top-k epilogue)");
+  e = launch_topk_merge_rows(reinterpret_cast<const int64_t*>(cand), m, tp.n_tiles * top_k, top_k, values, ids, s);
+  if (e != cudaSuccess) return cuda_fail(e, "top-k merge launch");
+  return KL_OK;
 }
 
 int kl_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,

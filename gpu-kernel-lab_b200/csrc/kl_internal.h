@@ -55,6 +55,12 @@ struct alignas(64) TcProblem {
   int m_tiles, n_tiles, kb_total;     // kb_total = k blocks per tile
   int y_transposed;
   int vec_store;                      // y 16-byte aligned, ldy % 8 == 0: 16-byte stores (1 row-major, 2 transposed)
+  // top-k epilogue (kl_linear_topk): instead of y, each (tile, token) writes its
+  // topk best (value, row + index_offset) candidates, packed, at
+  // cand[token * cand_ld + n_tile * topk + slot]
+  unsigned long long* cand;
+  long long index_offset;
+  int topk, cand_ld;
 };
 
 struct TcParams {
@@ -83,7 +89,9 @@ long long tc_problem_tiles(TcProblem& pr, int n_mma, int kblk, bool swiglu);
 // keeps every SM busy (fewer hand-offs per byte), else 128.
 int tc_choose_kblk(int fmt, int n_mma, long long units_at_256, int sm_count);
 TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count);
-cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
+// epilogue: 0 outputs, 1 SwiGLU outputs, 2 top-k candidates (TcProblem::cand)
+constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiTopk = 2;
+cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, int epi, bool xbf16, bool pdl, cudaStream_t s);
 
 // ---- dependent-chain decode GEMM: one 128-row tile per cluster (kl_tc_chain.cu)
 // For one int8 row-scale linear with M <= 64 launched after the op that
@@ -156,6 +164,7 @@ cudaError_t launch_topk_rows(const void* logits, bool xbf16, int rows, int n, lo
 // Qwen RMSNorm (kl_rmsnorm.cu); residual/residual_out both null for the plain norm
 cudaError_t launch_rmsnorm(const void* x, const void* residual, const void* weight, int dtype, int rows, int n,
                            float eps, int precise, void* y, void* residual_out, cudaStream_t s);
+// values == nullptr: ids receives the merged candidates packed (for a gather across ranks)
 cudaError_t launch_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
                                    cudaStream_t s);
 

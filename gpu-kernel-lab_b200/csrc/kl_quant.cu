@@ -320,8 +320,9 @@ cudaError_t launch_topk_rows(const void* logits, bool xbf16, int rows, int n, lo
 
 cudaError_t launch_topk_merge_rows(const int64_t* packed, int rows, int count, int top_k, float* values, int64_t* ids,
                                    cudaStream_t s) {
-  topk_merge_kernel<true, false><<<rows, kTopkThreads, 0, s>>>(nullptr, reinterpret_cast<const long long*>(packed),
-                                                               count, top_k, values, ids);
+  const long long* in = reinterpret_cast<const long long*>(packed);
+  if (values) topk_merge_kernel<true, false><<<rows, kTopkThreads, 0, s>>>(nullptr, in, count, top_k, values, ids);
+  else topk_merge_kernel<true, true><<<rows, kTopkThreads, 0, s>>>(nullptr, in, count, top_k, nullptr, ids);
   return cudaGetLastError();
 }
 

@@ -245,8 +245,44 @@ struct Cursor {
   }
 };
 
-template <int FMT, int NMMA, bool SWIGLU, bool XBF16>
+// 64-bit sort key of a candidate: order-preserving bits of the value rounded
+// to the output type (the selection compares the logits the layer would
+// output), then the inverted row, so that a larger key is the larger value
+// and, on ties, the lower index.  Key 0 is below every real candidate.
+KL_DEVICE unsigned long long topk_key(float v, int row) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
+}
+// The merge kernel's packed form: (index << 32) | f32 value bits.
+KL_DEVICE unsigned long long topk_packed(unsigned long long key, long long index_offset) {
+  if (key == 0ull) return (0x7FFFFFFFull << 32) | __float_as_uint(-INFINITY);   // no candidate
+  const uint32_t ord = static_cast<uint32_t>(key >> 32);
+  const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+  const long long row = static_cast<long long>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+  return (static_cast<unsigned long long>(row + index_offset) << 32) | u;
+}
+// Bitonic sort of one key per lane across the warp, descending (lane 0 holds the largest).
+KL_DEVICE unsigned long long warp_sort_desc(unsigned long long key) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
+      const bool desc = size == 32 || (lane & size) == 0;
+      const bool lower = (lane & stride) == 0;
+      const bool keep_max = lower == desc;
+      key = keep_max ? (key > other ? key : other) : (key < other ? key : other);
+    }
+  }
+  return key;
+}
+
+template <int FMT, int NMMA, int EPI, bool XBF16>
 struct Epi {
+  static constexpr bool SWIGLU = EPI == kEpiSwiglu;
+  static constexpr bool TOPK = EPI == kEpiTopk;
   // Physical weight row of tile row r (0..127) of n-tile nt.
   KL_DEVICE static int phys_row(const TcProblem& pr, int nt, int r) {
     if constexpr (SWIGLU) return r < 64 ? nt * 64 + r : pr.n_out + nt * 64 + (r - 64);
@@ -264,6 +300,32 @@ struct Epi {
   KL_DEVICE static void emit16(const TcProblem& pr, int mt, int nt, int r, int cb, const float (&v)[16], float* xch,
                                int g) {
     const int m0 = mt * NMMA + cb * 16;
+    if constexpr (TOPK) {
+      // per token, the tile's top-k rows: each warp sorts its 32 rows, then the
+      // group's first warp merges the four warps' best (all 128 threads call this)
+      const int n = nt * 128 + r;
+      const bool valid = n < pr.n_out;
+      const int lane = r & 31, wq = r >> 5, kk = pr.topk;
+      unsigned long long* xk = reinterpret_cast<unsigned long long*>(xch);   // [4 warps][16 tokens][8]
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (m0 + j < pr.m) {
+          const unsigned long long key = warp_sort_desc(valid ? topk_key(round_act<XBF16>(v[j]), n) : 0ull);
+          if (lane < kk) xk[(wq * 16 + j) * 8 + lane] = key;
+        }
+      }
+      named_bar_epi(g);
+      if (wq == 0) {
+#pragma unroll 1
+        for (int j = 0; j < 16 && m0 + j < pr.m; ++j) {
+          const unsigned long long key = warp_sort_desc(lane < 4 * kk ? xk[((lane / kk) * 16 + j) * 8 + lane % kk] : 0ull);
+          if (lane < kk)
+            pr.cand[static_cast<long long>(m0 + j) * pr.cand_ld + nt * kk + lane] = topk_packed(key, pr.index_offset);
+        }
+      }
+      named_bar_epi(g);
+      return;
+    }
     if constexpr (!SWIGLU) {
       // a warp's 32 rows x 16 tokens in range of a row-major output: stage them
       // [token][row] in this warp's 1 KB of the (otherwise idle) exchange area
@@ -332,12 +394,13 @@ struct Epi {
   }
 };
 
-template <int FMT, int NMMA, int KBL, bool SWIGLU, bool XBF16>
+template <int FMT, int NMMA, int KBL, int EPI, bool XBF16>
 __global__ void __launch_bounds__(TcRoles<FMT, NMMA, KBL>::THREADS, 1)
 tc_qgemm_kernel(const __grid_constant__ TcParams p) {
+  constexpr bool SWIGLU = EPI == kEpiSwiglu;
   using Cfg = TcCfg<NMMA, KBL>;
   using Roles = TcRoles<FMT, NMMA, KBL>;
-  using E = Epi<FMT, NMMA, SWIGLU, XBF16>;
+  using E = Epi<FMT, NMMA, EPI, XBF16>;
   static_assert(!grouped<FMT>() || KBL == 128 || (KBL == 256 && NMMA == 16), "4-bit group mode: one or two groups of 128 per stage");
   constexpr int WSB = w_stage_bytes<FMT, KBL>();
   constexpr bool ZST = zeros_in_stage<FMT, KBL>();
@@ -888,9 +951,9 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
-template <int FMT, int NMMA, int KBL, bool SWIGLU, bool XBF16>
+template <int FMT, int NMMA, int KBL, int EPI, bool XBF16>
 cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStream_t s) {
-  auto kern = tc_qgemm_kernel<FMT, NMMA, KBL, SWIGLU, XBF16>;
+  auto kern = tc_qgemm_kernel<FMT, NMMA, KBL, EPI, XBF16>;
   static std::atomic<int> smem_set[kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -916,7 +979,7 @@ cudaError_t launch_one(const TcParams& p, const TcPlan& plan, bool pdl, cudaStre
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int FMT, bool SWIGLU, bool XBF16>
+template <int FMT, int SWIGLU, bool XBF16>
 cudaError_t launch_nmma(const TcParams& p, const TcPlan& plan, bool pdl, cudaStream_t s) {
   if constexpr (FMT == KL_W8_ROW) {
     if (plan.kblk == 256) {
@@ -942,7 +1005,7 @@ cudaError_t launch_nmma(const TcParams& p, const TcPlan& plan, bool pdl, cudaStr
   }
 }
 
-template <bool SWIGLU, bool XBF16>
+template <int SWIGLU, bool XBF16>
 cudaError_t launch_fmt(const TcParams& p, const TcPlan& plan, int fmt, bool pdl, cudaStream_t s) {
   switch (fmt) {
     case KL_W8_ROW: return launch_nmma<KL_W8_ROW, SWIGLU, XBF16>(p, plan, pdl, s);
@@ -1023,9 +1086,12 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   return t;
 }
 
-cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, bool swiglu, bool xbf16, bool pdl, cudaStream_t s) {
-  if (swiglu) return xbf16 ? launch_fmt<true, true>(p, plan, fmt, pdl, s) : launch_fmt<true, false>(p, plan, fmt, pdl, s);
-  return xbf16 ? launch_fmt<false, true>(p, plan, fmt, pdl, s) : launch_fmt<false, false>(p, plan, fmt, pdl, s);
+cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, int epi, bool xbf16, bool pdl, cudaStream_t s) {
+  if (epi == kEpiSwiglu)
+    return xbf16 ? launch_fmt<kEpiSwiglu, true>(p, plan, fmt, pdl, s) : launch_fmt<kEpiSwiglu, false>(p, plan, fmt, pdl, s);
+  if (epi == kEpiTopk)   // selection over the logits of an lm_head: bf16 activations
+    return xbf16 ? launch_fmt<kEpiTopk, true>(p, plan, fmt, pdl, s) : cudaErrorInvalidValue;
+  return xbf16 ? launch_fmt<kEpiPlain, true>(p, plan, fmt, pdl, s) : launch_fmt<kEpiPlain, false>(p, plan, fmt, pdl, s);
 }
 
 }  // namespace kl

@@ -102,6 +102,33 @@ def quant_linear(x: torch.Tensor, weight, *, swiglu: bool = False, out: torch.Te
     return out
 
 
+def lm_head_topk(x: torch.Tensor, weight, k: int = 1, *, index_offset: int = 0, packed: bool = False):
+    """Top-``k`` rows of ``x @ dequant(weight)^T`` per token without writing the
+    logits: the tcgen05 GEMM's epilogue keeps each 128-row tile's best
+    candidates and a merge kernel reduces them (the reference's fused head,
+    ``learning/09_int4/kernels.py:37-50,77-99``, for M tokens and the int8 row
+    format).  Values are the logits rounded to x's dtype, as f32, descending;
+    ties go to the lower row.  Returns ``(values f32 [M, k], ids int64 [M, k])``
+    with ids offset by ``index_offset`` (a vocabulary shard's first row), or
+    with ``packed`` one int64 ``[M, k]`` tensor of ``id << 32 | value bits``.
+    x: [..., K] bf16; weight: int8 row format, or 4-bit with groups of 128
+    (at most 64 tokens)."""
+    fmt, data, scales, zeros, inverse, n, kdim, group = weight_spec(weight)
+    if torch.is_grad_enabled() and x.requires_grad:
+        raise ValueError("inference only")
+    if not x.is_cuda or data.device != x.device:
+        raise RuntimeError("x and the weight must be on the same CUDA device")
+    if x.shape[-1] != kdim or x.dtype != torch.bfloat16:
+        raise RuntimeError(f"x must be bf16 [..., {kdim}]")
+    if not 1 <= k <= min(8, n):
+        raise ValueError("k must be between 1 and min(8, vocabulary)")
+    x2 = x.reshape(-1, kdim)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    values, ids = torch.ops.kl_b200.linear_topk(x2, data, scales, zeros, fmt, group, k, index_offset, packed)
+    return ids if packed else (values, ids)
+
+
 class QuantLinear(nn.Module):
     """Bias-free ``nn.Linear`` replacement holding quantised weights only.
 

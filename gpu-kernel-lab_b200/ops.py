@@ -14,6 +14,8 @@ int8 ``[N, K]``, packed nibbles uint8 ``[N, K/2]`` or bf16 ``[N, K]``):
 
 * ``linear(x, data, scales, zeros, inverse, fmt, group, swiglu, transposed, flags) -> y``
 * ``linear_out(..., out)`` -- the same into a caller-owned ``out`` (CUDA graphs)
+* ``linear_topk(x, data, scales, zeros, fmt, group, top_k, index_offset, packed)
+  -> (values, ids)`` -- the fused lm_head top-k (no logits are written)
 * ``project(x, w, scales, inverse, group, warps, persistent, swiglu) -> y`` --
   the reference op's signature (``warp_gemv.cu:56-58``)
 * ``int4_gemv(x, data, scales, group, block_n) -> y`` and
@@ -40,6 +42,8 @@ _lib.define("linear_out(Tensor x, Tensor data, Tensor? scales, Tensor? zeros, Te
             "bool swiglu, bool transposed, int flags, Tensor(a!) out, Tensor? workspace=None) -> ()")
 _lib.define("project(Tensor x, Tensor w, Tensor? scales, Tensor? inverse, int group, int warps, bool persistent, "
             "bool swiglu) -> Tensor")
+_lib.define("linear_topk(Tensor x, Tensor data, Tensor? scales, Tensor? zeros, int fmt, int group, int top_k, "
+            "int index_offset=0, bool packed=False) -> (Tensor, Tensor)")
 _lib.define("int4_gemv(Tensor x, Tensor data, Tensor scales, int group, int block_n) -> Tensor")
 _lib.define("int4_lm_head_topk(Tensor x, Tensor data, Tensor scales, int group, int top_k, int block_n) "
             "-> (Tensor, Tensor)")
@@ -96,6 +100,32 @@ def _linear_out_fake(x, data, scales, zeros, inverse, fmt, group, swiglu, transp
     return None
 
 
+# ---- fused lm_head top-k ------------------------------------------------------------
+def _linear_topk_cuda(x, data, scales, zeros, fmt, group, top_k, index_offset=0, packed=False):
+    m, k = x.shape
+    n = data.shape[0]
+    lib = N.lib()
+    ids = torch.empty(m, top_k, dtype=torch.int64, device=x.device)
+    values = torch.empty(0 if packed else m * top_k, dtype=torch.float32, device=x.device).view(-1, top_k)
+    with torch.cuda.device(x.device):
+        need = lib.kl_linear_topk_workspace_bytes(m, n, k, fmt, top_k)
+        ws = N.workspace(x.device, need, stream=torch.cuda.current_stream(x.device))
+        N.check(lib.kl_linear_topk(N.ptr(x), N.act_dtype_code(x.dtype), m, k, N.ptr(data), fmt, n, group,
+                                   N.ptr(scales), N.ptr(zeros), top_k, index_offset,
+                                   None if packed else N.ptr(values), N.ptr(ids), N.ptr(ws),
+                                   0 if ws is None else ws.numel(), 0, N.stream_handle(x.device)))
+    return values, ids
+
+
+_lib.impl("linear_topk", _linear_topk_cuda, "CUDA")
+
+
+@torch.library.register_fake("kl_b200::linear_topk")
+def _linear_topk_fake(x, data, scales, zeros, fmt, group, top_k, index_offset=0, packed=False):
+    m = x.shape[0]
+    return x.new_empty((0 if packed else m, top_k), dtype=torch.float32), x.new_empty((m, top_k), dtype=torch.int64)
+
+
 # ---- project (the reference op) ---------------------------------------------------
 def _project_cuda(x, w, scales, inverse, group, warps, persistent, swiglu):
     n, k = w.shape
@@ -119,6 +149,10 @@ def _project_fake(x, w, scales, inverse, group, warps, persistent, swiglu):
 # ---- int4 -------------------------------------------------------------------------
 def _int4_gemv_cuda(x, data, scales, group, block_n):
     n, k = data.shape[0], x.numel()
+    if group == 128 and k % 128 == 0 and x.dtype == torch.bfloat16:
+        # the tcgen05 kernel, on the plan the fused head uses: its values are
+        # exactly the logits this returns (the reference shares _project too)
+        return _linear_cuda(x.view(1, k), data, scales, None, None, N.KL_W4_SYM, group).view(n)
     y = torch.empty(n, device=x.device, dtype=x.dtype)
     with torch.cuda.device(x.device):
         N.check(N.lib().kl_int4_gemv(N.ptr(x), N.act_dtype_code(x.dtype), k, N.ptr(data), N.ptr(scales), n,
@@ -131,11 +165,12 @@ def _int4_head_cuda(x, data, scales, group, top_k, block_n):
     lib = N.lib()
     values = torch.empty(top_k, device=x.device, dtype=torch.float32)
     ids = torch.empty(top_k, device=x.device, dtype=torch.int64)
-    need = lib.kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n)
-    ws = torch.empty(need, dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
+        need = max(lib.kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n),
+                   lib.kl_linear_topk_workspace_bytes(1, n, k, N.KL_W4_SYM, top_k))
+        ws = N.workspace(x.device, need, stream=torch.cuda.current_stream(x.device))
         N.check(lib.kl_int4_lm_head_topk(N.ptr(x), N.act_dtype_code(x.dtype), k, N.ptr(data), N.ptr(scales), n,
-                                         group, top_k, block_n, N.ptr(values), N.ptr(ids), N.ptr(ws), need,
+                                         group, top_k, block_n, N.ptr(values), N.ptr(ids), N.ptr(ws), ws.numel(),
                                          N.stream_handle(x.device)), ValueError)
     return values, ids
 
@@ -154,4 +189,4 @@ def _int4_head_fake(x, data, scales, group, top_k, block_n):
     return x.new_empty(top_k, dtype=torch.float32), x.new_empty(top_k, dtype=torch.int64)
 
 
-OPS = ("linear", "linear_out", "project", "int4_gemv", "int4_lm_head_topk")
+OPS = ("linear", "linear_out", "linear_topk", "project", "int4_gemv", "int4_lm_head_topk")

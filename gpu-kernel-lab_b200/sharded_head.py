@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import _native as N
-from .linear import QuantLinear, quant_linear
+from .linear import QuantLinear, lm_head_topk, quant_linear
 
 
 def topk_rows(logits: torch.Tensor, k: int, index_offset: int = 0, *, packed: bool = False):
@@ -48,6 +48,18 @@ def topk_merge_rows(packed: torch.Tensor, k: int):
     N.check(N.lib().kl_topk_merge_rows(N.ptr(packed), rows, count, k, N.ptr(out_v), N.ptr(out_i),
                                        N.stream_handle(packed.device)))
     return out_v, out_i
+
+
+def _fused_local_topk(x, w, k, offset):
+    """This shard's top-k per token, packed, from the fused lm_head top-k (no
+    logits written); shapes or formats the tcgen05 kernel does not take
+    compute the shard's logits and select from them."""
+    try:
+        return lm_head_topk(x, w, k, index_offset=offset, packed=True)
+    except N.NativeError as e:
+        if e.status != N.KL_ERR_UNSUPPORTED:
+            raise
+    return topk_rows(quant_linear(x, w), k, offset, packed=True)
 
 
 def shard_bounds(vocab: int, world: int, rank: int) -> tuple[int, int]:
@@ -83,7 +95,7 @@ class VocabShardedHead:
         self.weight = weight_shard
         self.project = project or (lambda x, w, out: quant_linear(x, w, transposed=True, out=out))
         # local_topk(x, w, k, offset) -> packed int64 [M, k]; merge_topk(packed [M, G*k], k) -> (values, ids)
-        self.local_topk = local_topk or (lambda x, w, k, offset: topk_rows(quant_linear(x, w), k, offset, packed=True))
+        self.local_topk = local_topk or _fused_local_topk
         self.merge_topk = merge_topk or topk_merge_rows
 
     @classmethod

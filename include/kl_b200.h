@@ -161,7 +161,12 @@ int kl_int4_gemv(const void* x, int x_dtype, int k, const uint8_t* w, const floa
  * int4_lm_head_topk(x, packed, top_k, block_n): fused lm_head projection with
  * tile-local top-k and a global merge.  values f32 [top_k], ids int64 [top_k]
  * (descending; top-1 ties resolve to the lowest vocabulary index).
- * workspace: kl_int4_lm_head_topk_workspace_bytes(n, top_k, block_n) bytes.
+ * With bf16 x and groups of 128 it runs kl_linear_topk (the logits are never
+ * written); other shapes write the logits into the workspace and select.
+ * workspace: the larger of kl_int4_lm_head_topk_workspace_bytes(n, top_k,
+ * block_n) and, for the fused path, kl_linear_topk_workspace_bytes(1, n, k,
+ * KL_W4_SYM, top_k) bytes, under kl_linear's workspace rule (its first 64 KiB
+ * zero before the first use; the calls leave it zero).
  */
 int kl_int4_lm_head_topk(const void* x, int x_dtype, int k, const uint8_t* w,
                          const float* scales, int n, int group, int top_k, int block_n,
@@ -183,6 +188,29 @@ int kl_quantize_w4(const void* w, int w_dtype, int n, int k, int group, int w_fo
 int kl_dequantize(const void* w, int w_format, int n, int k, int group,
                   const void* scales, const void* zeros, const float* inverse,
                   float* out, void* stream);
+
+/*
+ * Fused lm_head top-k (learning/09_int4/kernels.py:37-50 _head_candidates and
+ * :77-99 int4_lm_head_topk, generalised to M tokens, the int8 row format and
+ * a vocabulary shard): the logits x @ dequant(w)^T are never written.  Each
+ * 128-row tile of the tcgen05 GEMM selects, per token, its top_k rows in the
+ * epilogue (values rounded to bf16 as the logits would be, value descending,
+ * the lower row first on ties) and a merge kernel reduces the tiles'
+ * candidates.
+ *   x bf16 [M, K]; w KL_W8_ROW, or KL_W4_SYM / KL_W4_ASYM with group 128 and
+ *   M <= 64; 1 <= top_k <= min(8, N); ids are row + index_offset (a shard's
+ *   first vocabulary row).
+ *   values f32 [M, top_k] and ids int64 [M, top_k]; with values == NULL, ids
+ *   receives packed candidates (row << 32 | f32 value bits), the form
+ *   kl_topk_merge_rows takes after a gather across ranks.
+ *   workspace: kl_linear_topk_workspace_bytes(...) bytes; its first 64 KiB
+ *   follow kl_linear's workspace rule (zero before the first use).
+ * Returns KL_ERR_UNSUPPORTED for shapes the tcgen05 kernel does not take.
+ */
+size_t kl_linear_topk_workspace_bytes(int m, int n, int k, int w_format, int top_k);
+int kl_linear_topk(const void* x, int x_dtype, int m, int k, const void* w, int w_format, int n, int group,
+                   const void* scales, const void* zeros, int top_k, long long index_offset, float* values,
+                   int64_t* ids, void* workspace, size_t workspace_bytes, int flags, void* stream);
 
 /* ---- diagnostics -------------------------------------------------------- */
 const char* kl_status_string(int status);
