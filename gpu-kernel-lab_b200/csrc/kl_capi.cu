@@ -267,11 +267,6 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
   if (tc && prefill_applies(m, k, w_format, di.sm_count)) {
     PfParams p;
     std::memset(&p, 0, sizeof(p));
-    rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc != KL_OK) return rc;
-    rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m,
-                   static_cast<uint64_t>(k) * eb, 64, 96, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != KL_OK) return rc;
     p.scales = scales;
     p.y = y;
     p.ldy = transposed ? m : n_out;
@@ -282,7 +277,13 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     p.y_transposed = transposed ? 1 : 0;
     p.vec_store = (aligned16(y) && p.ldy % 8 == 0) ? (transposed ? 2 : 1) : 0;
     p.status = di.status;
-    prefill_tiles(p, swiglu != 0);
+    prefill_tiles(p, swiglu != 0, di.sm_count);
+    rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != KL_OK) return rc;
+    // each CTA of a pair loads half of the tile's tokens
+    rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m,
+                   static_cast<uint64_t>(k) * eb, 64, static_cast<uint32_t>(p.tok / 2), CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != KL_OK) return rc;
     const cudaError_t e = launch_prefill(p, prefill_grid(p, di.sm_count), swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 pair GEMM launch");
     return KL_OK;
@@ -780,12 +781,12 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     pf.n = n;
     pf.k = k;
     pf.n_out = swiglu ? n / 2 : n;
-    prefill_tiles(pf, swiglu != 0);
+    prefill_tiles(pf, swiglu != 0, sm_count);
     out[0] = 3;
     out[1] = prefill_grid(pf, sm_count);
     out[2] = prefill_threads();
-    out[3] = prefill_smem_bytes();
-    out[4] = 192;                       // tokens per tile (pair MMA N)
+    out[3] = prefill_smem_bytes(pf.tok);
+    out[4] = pf.tok;                    // tokens per tile (pair MMA N)
     out[5] = 8;                         // weight stages
     out[6] = pf.n_tiles * pf.m_tiles;
     out[7] = pf.n_tiles * pf.m_tiles * pf.kb_total;

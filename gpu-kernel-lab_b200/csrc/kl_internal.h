@@ -127,20 +127,22 @@ cudaError_t launch_chain(const ChainParams& p, const ChainPlan& plan, bool swigl
 constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel
 struct PfParams {
   CUtensorMap tmap_w;                 // int8 [N, K], box 64 x 64 rows, 64B swizzle
-  CUtensorMap tmap_x;                 // bf16/f16 [M, K], box 64 x 96 rows, 128B swizzle
+  CUtensorMap tmap_x;                 // bf16/f16 [M, K], box 64 x (tok / 2) rows, 128B swizzle
   const void* scales;                 // bf16 [N]
   void* y;
   long long ldy;
   int m, n, k, n_out;
   int n_tiles, m_tiles, kb_total;
+  int tok;                            // tokens per tile: 192, 128 or 64 (the x tensor map's box is tok / 2 rows)
   int y_transposed;
   int vec_store;                      // y 16-byte aligned, ldy % 8 == 0: 16-byte stores (1 row-major, 2 transposed)
   int* status;
 };
 int prefill_threads();
-int prefill_smem_bytes();
+int prefill_smem_bytes(int tok);
 int prefill_k_block();
-void prefill_tiles(PfParams& p, bool swiglu);
+int prefill_choose_tokens(int m, int n_tiles, int sm_count);
+void prefill_tiles(PfParams& p, bool swiglu, int sm_count);
 int prefill_grid(const PfParams& p, int sm_count);
 cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 

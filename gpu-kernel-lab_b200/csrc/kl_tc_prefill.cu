@@ -23,6 +23,8 @@
 // only; every wait is bounded (kWaitLimitNs) and records KL_ERR_TIMEOUT.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "kl_common.cuh"
 #include "kl_internal.h"
 
@@ -31,13 +33,13 @@ namespace {
 
 constexpr int kPfKb = 64;                        // K elements per stage
 constexpr int kPfRows = 128;                     // weight rows per CTA
-constexpr int kPfTokens = 192;                   // tokens per tile (MMA N)
-constexpr int kPfHalf = kPfTokens / 2;           // tokens per CTA
+constexpr int kPfMaxTokens = 192;                // tokens per tile (MMA N): 192, 128 or 64
 constexpr int kPfW = 8;                          // weight stages
 constexpr int kPfX = 8;                          // token stages
 constexpr int kPfA = 4;                          // TMEM A stages
 constexpr int kPfWStage = kPfRows * kPfKb;       // 8 KB of int8
-constexpr int kPfXStage = kPfHalf * kPfKb * 2;   // 12 KB of bf16
+// token stage of one CTA: half the tile's tokens x 64 bf16 (12 KB at 192 tokens)
+__host__ __device__ constexpr int pf_xstage(int tok) { return (tok / 2) * kPfKb * 2; }
 constexpr int kPfACols = kPfKb / 2;              // TMEM columns per A stage
 constexpr int kPfDCol0 = kPfA * kPfACols;        // 128
 constexpr int kPfConv = 8;
@@ -47,16 +49,16 @@ constexpr int kPfChunk = 32;                     // tokens per epilogue step
 constexpr int kPfXchHalf = 64 * (kPfChunk / 2 + 1);  // one direction of the SwiGLU exchange (padded rows)
 constexpr int kPfXchFloats = 2 * kPfXchHalf;
 constexpr int kPfStageBytes = 32 * kPfChunk * 2; // per epilogue warp: 32 rows x 32 tokens, bf16
-static_assert(kPfDCol0 + 2 * kPfTokens == 512, "TMEM budget");
+static_assert(kPfDCol0 + 2 * kPfMaxTokens == 512, "TMEM budget");
 
 struct PfLayout {
   uint32_t w, x, xch, stage, bars, misc, total;
 };
-constexpr PfLayout pf_layout() {
+constexpr PfLayout pf_layout(int tok) {
   PfLayout l{};
   l.w = 0;
   l.x = l.w + kPfW * kPfWStage;
-  l.xch = l.x + kPfX * kPfXStage;
+  l.xch = l.x + kPfX * pf_xstage(tok);
   l.stage = l.xch + kPfXchFloats * 4;
   l.bars = l.stage + 4 * kPfStageBytes;
   // w_full, w_empty [W]; x_full, x_empty [X]; a_full, a_empty [A]; d_full, d_empty [2]; done
@@ -136,11 +138,15 @@ KL_DEVICE void pf_emit(const PfParams& p, uint8_t* stage, int col0, int ncols, i
   }
 }
 
-template <bool SWIGLU, bool XBF16>
+template <bool SWIGLU, bool XBF16, int TOK>
 __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_constant__ PfParams p) {
+  constexpr int kPfTokens = TOK;                 // tokens per tile (MMA N)
+  constexpr int kPfHalf = TOK / 2;               // tokens per CTA
+  constexpr int kPfXStage = pf_xstage(TOK);
+  static_assert(TOK % kPfChunk == 0 && TOK <= kPfMaxTokens, "token tile");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr PfLayout L = pf_layout();
+  constexpr PfLayout L = pf_layout(TOK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -376,10 +382,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   if (warp == 2) tmem_dealloc_pair(tmem, 512);
 }
 
-template <bool SWIGLU, bool XBF16>
+template <bool SWIGLU, bool XBF16, int TOK>
 cudaError_t launch_pf(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
-  auto kern = tc_prefill_kernel<SWIGLU, XBF16>;
-  constexpr int smem = static_cast<int>(pf_layout().total);
+  auto kern = tc_prefill_kernel<SWIGLU, XBF16, TOK>;
+  constexpr int smem = static_cast<int>(pf_layout(TOK).total);
   static bool attr[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -425,12 +431,35 @@ cudaError_t launch_pf(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
 }  // namespace
 
 int prefill_threads() { return kPfThreads; }
-int prefill_smem_bytes() { return static_cast<int>(pf_layout().total); }
+int prefill_smem_bytes(int tok) { return static_cast<int>(pf_layout(tok).total); }
 int prefill_k_block() { return kPfKb; }
 
-void prefill_tiles(PfParams& p, bool swiglu) {
+// Tokens per tile: the tile count of each choice is spread over the CTA pairs
+// in waves; a tile costs about (tile tokens + 48) token-steps of MMA and
+// epilogue, but never less than 192, because converting the tile's weights
+// takes the same time per K block whatever the token count (measured: 128-token
+// tiles ran at about the pace of 192-token ones).  The lowest waves x cost wins,
+// the larger tile on ties.
+int prefill_choose_tokens(int m, int n_tiles, int sm_count) {
+  const int pairs = std::max(1, sm_count / 2);
+  int best = kPfMaxTokens;
+  long long best_cost = -1;
+  for (int tok : {192, 128, 64}) {
+    const long long tiles = static_cast<long long>(n_tiles) * ((m + tok - 1) / tok);
+    const long long waves = (tiles + pairs - 1) / pairs;
+    const long long cost = waves * std::max(tok + 48, 192);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = tok;
+    }
+  }
+  return best;
+}
+
+void prefill_tiles(PfParams& p, bool swiglu, int sm_count) {
   p.n_tiles = swiglu ? (p.n_out + 127) / 128 : (p.n + 255) / 256;
-  p.m_tiles = (p.m + kPfTokens - 1) / kPfTokens;
+  p.tok = prefill_choose_tokens(p.m, p.n_tiles, sm_count);
+  p.m_tiles = (p.m + p.tok - 1) / p.tok;
   p.kb_total = p.k / kPfKb;
 }
 
@@ -440,9 +469,19 @@ int prefill_grid(const PfParams& p, int sm_count) {
   return 2 * pairs;
 }
 
+template <bool SWIGLU, bool XBF16>
+cudaError_t launch_tok(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
+  switch (p.tok) {
+    case 192: return launch_pf<SWIGLU, XBF16, 192>(p, grid, pdl, s);
+    case 128: return launch_pf<SWIGLU, XBF16, 128>(p, grid, pdl, s);
+    case 64: return launch_pf<SWIGLU, XBF16, 64>(p, grid, pdl, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s) {
-  if (swiglu) return xbf16 ? launch_pf<true, true>(p, grid, pdl, s) : launch_pf<true, false>(p, grid, pdl, s);
-  return xbf16 ? launch_pf<false, true>(p, grid, pdl, s) : launch_pf<false, false>(p, grid, pdl, s);
+  if (swiglu) return xbf16 ? launch_tok<true, true>(p, grid, pdl, s) : launch_tok<true, false>(p, grid, pdl, s);
+  return xbf16 ? launch_tok<false, true>(p, grid, pdl, s) : launch_tok<false, false>(p, grid, pdl, s);
 }
 
 }  // namespace kl

@@ -53,6 +53,20 @@ def test_validation_needs_no_gpu(kl):
     assert lib.kl_int4_gemv(fake, 0, 128, fake, fake, 8, 128, 24, fake, None) == N.KL_ERR_INVALID
 
 
+def prefill_tokens(m, n_tiles, sm=148):
+    """Restatement of the pair kernel's token-tile choice: the tile count of
+    each choice in waves over the CTA pairs, times max(tile tokens + 48, 192);
+    the lowest cost wins, the larger tile on ties."""
+    pairs = max(1, sm // 2)
+    best, best_cost = 192, None
+    for tok in (192, 128, 64):
+        tiles = n_tiles * -(-m // tok)
+        cost = -(-tiles // pairs) * max(tok + 48, 192)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = tok, cost
+    return best
+
+
 def chain_plan(m, n, k, swiglu=False, sm=148):
     """Restatement of the host planner of the single-tile cluster kernel: the
     fewest 128-wide K blocks per CTA from 2 to 4 that keep the cluster portable
@@ -82,8 +96,9 @@ def test_plan_partition_w8(kl, m, n, k):
     # M >= 256 with K a multiple of 64 runs on the CTA-pair prefill kernel
     if m >= 256 and k % 64 == 0:
         assert plan["kernel"] == 3
-        assert plan["grid"] % 2 == 0 and plan["n_mma"] == 192 and 1 <= plan["grid"] <= 148
-        assert plan["tiles"] == ((n + 255) // 256) * ((m + 191) // 192)
+        tok = prefill_tokens(m, (n + 255) // 256)
+        assert plan["grid"] % 2 == 0 and plan["n_mma"] == tok and 1 <= plan["grid"] <= 148
+        assert plan["tiles"] == ((n + 255) // 256) * ((m + tok - 1) // tok)
     elif chain is not None:
         # one decode linear small enough for the single-tile cluster kernel
         assert plan["kernel"] == 4
@@ -127,7 +142,9 @@ def test_chain_plan_config1_shapes(kl):
 def test_plan_partition_swiglu(kl, m, n, k):
     plan = kl._native.describe_plan(m, n, k, kl._native.KL_W8_ROW, swiglu=True, sm_count=148)
     if m >= 256:
-        assert plan["kernel"] == 3 and plan["tiles"] == ((n // 2 + 127) // 128) * ((m + 191) // 192)
+        tok = prefill_tokens(m, (n // 2 + 127) // 128)
+        assert plan["kernel"] == 3 and plan["n_mma"] == tok
+        assert plan["tiles"] == ((n // 2 + 127) // 128) * ((m + tok - 1) // tok)
     elif chain_plan(m, n, k, swiglu=True) is not None:
         assert plan["kernel"] == 4 and plan["tiles"] == (n // 2 + 63) // 64
     else:
@@ -171,3 +188,17 @@ def test_simt_plan_for_reference_formats(kl):
     assert N.describe_plan(1, 34, 256, N.KL_W8_GROUP)["kernel"] == 1
     assert N.describe_plan(1, 33, 7, N.KL_BF16_DENSE)["kernel"] == 1
     assert N.describe_plan(1, 17, 128, N.KL_W4_SYM, flags=N.KL_FLAG_FORCE_SIMT)["kernel"] == 1
+
+
+def test_prefill_token_tiles_fill_the_pairs():
+    """The N = 1024 GEMMs of a 2048-token prefill take 128-token tiles (64 tiles
+    for 74 pairs instead of 44 at 192); the wide ones keep 192."""
+    N_ = None
+    from tests.conftest import load_kl
+    N_ = load_kl()._native
+    assert N_.describe_plan(2048, 1024, 2048, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 128
+    assert N_.describe_plan(2048, 1024, 3072, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 128
+    assert N_.describe_plan(8192, 4096, 1024, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 192
+    assert N_.describe_plan(8192, 1024, 2048, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 192
+    assert N_.describe_plan(2048, 4096, 1024, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 192
+    assert N_.describe_plan(512, 1024, 2048, N_.KL_W8_ROW, sm_count=148)["n_mma"] == 128
