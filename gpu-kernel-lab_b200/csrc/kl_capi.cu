@@ -289,6 +289,31 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     return KL_OK;
   }
 
+  if (tc && w_format == KL_W8_ROW && !(flags & (KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC))) {
+    // One or two tokens: full rows per CTA on CUDA cores, nothing exchanged
+    // between CTAs (the shortest path after the dependency wait)
+    const GemvChainPlan gp = plan_gemv_chain(m, n, k, swiglu != 0, di.sm_count);
+    if (gp.ok) {
+      GemvChainParams c;
+      std::memset(&c, 0, sizeof(c));
+      c.w = static_cast<const int8_t*>(w);
+      c.scales = scales;
+      c.x = x;
+      c.y = y;
+      c.ldy = transposed ? m : n_out;
+      c.m = m;
+      c.k = k;
+      c.n = n;
+      c.n_out = n_out;
+      c.rows = gp.rows;
+      c.y_transposed = transposed ? 1 : 0;
+      c.status = di.status;
+      const cudaError_t e = launch_gemv_chain(c, gp, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
+      if (e != cudaSuccess) return cuda_fail(e, "chain GEMV launch");
+      return KL_OK;
+    }
+  }
+
   if (tc && w_format == KL_W8_ROW && !(flags & KL_FLAG_PERSISTENT)) {
     // One decode-size linear: the single-tile cluster kernel, whose fixed cost
     // after the previous kernel in the stream is a fraction of the persistent one's.
@@ -793,6 +818,23 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     if (out[1] % 2 || out[1] > (sm_count & ~1) || out[3] > 227 * 1024)
       return fail(KL_ERR_INVALID, "pair plan out of range");
     return KL_OK;
+  }
+  if (w_format == KL_W8_ROW && !(flags & (KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC))) {
+    const GemvChainPlan gp = plan_gemv_chain(m, n, k, swiglu != 0, sm_count);
+    if (gp.ok) {
+      out[0] = 5;
+      out[1] = gp.grid;
+      out[2] = 256;
+      out[3] = gp.smem;
+      out[4] = gp.mt;
+      out[5] = 1;
+      out[6] = gp.rows;
+      out[7] = gp.grid;
+      const int n_out = swiglu ? n / 2 : n;
+      if (gp.grid * gp.rows < n_out || (gp.grid - 1) * gp.rows >= n_out || gp.rows > 32 || gp.smem > 227 * 1024)
+        return fail(KL_ERR_INVALID, "chain GEMV plan out of range");
+      return KL_OK;
+    }
   }
   if (w_format == KL_W8_ROW && !(flags & KL_FLAG_PERSISTENT)) {
     const ChainPlan cp = plan_chain(m, n, k, swiglu != 0, sm_count);

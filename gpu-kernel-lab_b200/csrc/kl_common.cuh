@@ -74,6 +74,12 @@ KL_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int3
       " [%0], [%1, {%2, %3}], [%4];"
       :: "r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, counted on an mbarrier.
+KL_DEVICE void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
 // Prefetch a tile of a tensor into L2 (no shared memory, no completion signal).
 KL_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" :: "l"(map), "r"(x), "r"(y) : "memory");
@@ -356,6 +362,45 @@ KL_DEVICE uint32_t u4x2_to_f16x2(uint32_t w, uint32_t s, uint32_t sel, uint32_t 
   const uint32_t t = prmt(w, s, sel);
   const uint32_t m = lop3<0x6A>(t, 0x000F000Fu, magic_xor);
   return fma_f16x2(m, 0x3C003C00u, bias);
+}
+
+// Transposing warp reduction of V (power of two <= 32) values.  Afterwards the
+// lane `l` holds the full sum of value index ((l >> (5 - log2 V)) restricted) --
+// see value_index_of_lane.
+template <int V>
+KL_DEVICE float warp_reduce_multi(float (&v)[V]) {
+  const int lane = threadIdx.x & 31;
+  int cnt = V;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (cnt > 1) {
+      const bool upper = (lane & off) != 0;
+      const int half = cnt >> 1;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? v[i] : v[i + half];
+          const float keep = upper ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      cnt = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+  return v[0];
+}
+template <int V>
+KL_DEVICE int value_index_of_lane(int lane) {
+  // index bits are taken from lane bits 4, 3, ... (most significant first)
+  int idx = 0, cnt = V, bit = 16;
+  while (cnt > 1) {
+    idx += (lane & bit) ? (cnt >> 1) : 0;
+    cnt >>= 1;
+    bit >>= 1;
+  }
+  return idx;
 }
 
 KL_DEVICE uint32_t pack_bf16x2(float lo, float hi) {

@@ -77,45 +77,6 @@ KL_DEVICE void decode8(const uint4& c, int q, float zbias, float (&v)[8]) {
   }
 }
 
-// Transposing warp reduction of V (power of two <= 32) values.  Afterwards the
-// lane `l` holds the full sum of value index ((l >> (5 - log2 V)) restricted) --
-// see value_index_of_lane.
-template <int V>
-KL_DEVICE float warp_reduce_multi(float (&v)[V]) {
-  const int lane = threadIdx.x & 31;
-  int cnt = V;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    if (cnt > 1) {
-      const bool upper = (lane & off) != 0;
-      const int half = cnt >> 1;
-#pragma unroll
-      for (int i = 0; i < V / 2; ++i) {
-        if (i < half) {
-          const float send = upper ? v[i] : v[i + half];
-          const float keep = upper ? v[i + half] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-      }
-      cnt = half;
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-    }
-  }
-  return v[0];
-}
-template <int V>
-KL_DEVICE int value_index_of_lane(int lane) {
-  // index bits are taken from lane bits 4, 3, ... (most significant first)
-  int idx = 0, cnt = V, bit = 16;
-  while (cnt > 1) {
-    idx += (lane & bit) ? (cnt >> 1) : 0;
-    cnt >>= 1;
-    bit >>= 1;
-  }
-  return idx;
-}
-
 // Shared-memory index of activation element k for the lane-interleaved layout.
 template <int CE>
 KL_DEVICE int xs_index(int k) {

@@ -1,0 +1,296 @@
+// CUDA-core decode linear for ONE or TWO tokens inside a dependent chain (a
+// model forward: every linear waits for the op that produced its input; the
+// call pattern of profiling/decode_stage2_ablation.py:78-143 around the op of
+// learning/10_cuda_decode/warp_gemv.cu:56-90, whose per-row warp GEMV this
+// replaces for the int8 row format).
+//
+//   y[m, n] = scale[n] * sum_k x[m, k] * q[n, k]      (f32 accumulate, bf16/f16 out)
+//
+// For one or two tokens the arithmetic is small (4 M multiply-adds for a 4 MB
+// QKV, spread over the SMs) and the time of a dependent linear is latency.
+// The tensor-core path pays, after the dependency wait, for the activation
+// copy, the MMA issue, the TMEM read and a K-split exchange between CTAs; this
+// kernel keeps only what must follow the wait:
+//
+//   * Each CTA owns `rows` output rows with all of K (gate and up rows of a
+//     SwiGLU pair together), so nothing is exchanged between CTAs.
+//   * Before the wait: one bulk copy of the CTA's weight rows (contiguous in
+//     the [N, K] layout) into shared memory, and the row scales into registers.
+//     The dependent kernel is triggered first, so the next linear's CTAs can
+//     start and fetch their weights while this one waits and computes.
+//   * After the wait: the activations (2 KB per token at K = 1024) are staged
+//     in shared memory once; each warp takes its rows, each lane a strided
+//     set of 16-element K chunks: exact int8 -> f32 (the 2^23 magic number),
+//     packed f32x2 multiply-adds against the activations kept in registers
+//     across the warp's rows, one warp reduction per output, scale and store.
+//
+// Every wait is bounded; on expiry the kernel records KL_ERR_TIMEOUT and
+// waits (bounded) for its own copy before returning.
+#include "kl_common.cuh"
+#include "kl_internal.h"
+
+#include <algorithm>
+#include <atomic>
+
+namespace kl {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kRpw = 4;                          // output rows per warp (at most)
+
+KL_DEVICE unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+KL_DEVICE float sum2(unsigned long long v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+KL_DEVICE void ffma2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+KL_DEVICE unsigned long long fsub2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// 16 int8 weights -> 8 f32 pairs (elements 2e, 2e+1).  Byte j of
+// (word ^ 0x80808080) placed under the exponent bits 0x4B00 is the f32 2^23 + u
+// with u = q + 128; one packed subtract of 2^23 + 128 per pair leaves q exactly.
+KL_DEVICE void w16_to_f32x2(const uint4& v, unsigned long long (&w)[8]) {
+  const uint32_t wd[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+  const unsigned long long bias = pack2(8388736.0f, 8388736.0f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    unsigned long long a, b;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "r"(prmt(wd[i], 0x4B000000u, 0x7540u)), "r"(prmt(wd[i], 0x4B000000u, 0x7541u)));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "r"(prmt(wd[i], 0x4B000000u, 0x7542u)), "r"(prmt(wd[i], 0x4B000000u, 0x7543u)));
+    w[2 * i] = fsub2(a, bias);
+    w[2 * i + 1] = fsub2(b, bias);
+  }
+}
+// 8 activations (one 16-byte chunk) -> 4 f32 pairs.
+template <bool XBF16>
+KL_DEVICE void x8_to_f32x2(const uint4& v, unsigned long long* out) {
+  const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (XBF16) {
+      out[i] = pack2(__uint_as_float(wd[i] << 16), __uint_as_float(wd[i] & 0xFFFF0000u));
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&wd[i]);
+      out[i] = pack2(__low2float(h), __high2float(h));
+    }
+  }
+}
+
+// s[i] for a runtime i < kRpw without indexing the register array dynamically.
+KL_DEVICE float sc_sel(const float (&s)[kRpw], int i) {
+  float r = s[0];
+#pragma unroll
+  for (int j = 1; j < kRpw; ++j) r = i == j ? s[j] : r;
+  return r;
+}
+
+KL_DEVICE bool wait_bounded(uint32_t bar, int* status) {
+  if (mbar_try_wait(bar, 0)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, 0)) return true;
+    if ((spin & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+      record_error(status, KL_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+template <int MT, bool SWIGLU, bool XBF16>
+__global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_constant__ GemvChainParams p) {
+  constexpr int H = SWIGLU ? 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int k = p.k, R = p.rows;
+  const int r0 = blockIdx.x * R;
+  const int nr = min(R, p.n_out - r0);                   // output rows of this CTA
+  uint8_t* wsm = smem;                                   // [H][R][K] int8
+  uint8_t* xs = smem + static_cast<size_t>(H) * R * k;   // [MT][K] activations (bf16/f16)
+  const uint32_t bar = smem_u32(xs + static_cast<size_t>(MT) * k * 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    const uint32_t bytes = static_cast<uint32_t>(nr) * k;
+    mbar_arrive_expect_tx(bar, H * bytes);
+    // weights are static: fetch them while the previous kernel runs
+    bulk_copy_g2s(smem_u32(wsm), p.w + static_cast<size_t>(r0) * k, bytes, bar);
+    if constexpr (SWIGLU)
+      bulk_copy_g2s(smem_u32(wsm + static_cast<size_t>(R) * k), p.w + static_cast<size_t>(p.n_out + r0) * k, bytes,
+                    bar);
+  }
+  __syncthreads();                                       // barrier initialised before anyone waits on it
+  pdl_launch_dependents();
+  float sc[kRpw], scu[kRpw];
+#pragma unroll
+  for (int i = 0; i < kRpw; ++i) {
+    const int row = warp + kWarps * i;
+    const __nv_bfloat16* s = reinterpret_cast<const __nv_bfloat16*>(p.scales);
+    sc[i] = row < nr ? __bfloat162float(s[r0 + row]) : 0.f;
+    scu[i] = (SWIGLU && row < nr) ? __bfloat162float(s[p.n_out + r0 + row]) : 0.f;
+  }
+  void* y_ptr = p.y;
+  long long ldy = p.ldy;
+  int y_tr = p.y_transposed, m = p.m;
+  asm volatile("" : "+l"(y_ptr), "+l"(ldy), "+r"(y_tr), "+r"(m));
+  const int kc = k / 8;
+  const char* xg = static_cast<const char*>(p.x);
+  // Warm L2 with the activations' lines now: they are only read after the
+  // dependency wait, but L2 is where global memory is coherent, so a line the
+  // previous kernel rewrites in the meantime is read fresh all the same.
+  for (int c = threadIdx.x * 8; c < kc; c += kThreads * 8)
+    for (int t = 0; t < m; ++t)
+      asm volatile("prefetch.global.L2 [%0];" :: "l"(xg + (static_cast<size_t>(t) * k + c * 8) * 2));
+
+  pdl_wait();                                            // the activations come from the previous kernel
+  // ---- stage the activations: every token row's 16-byte chunks, all loads in flight
+  for (int c = threadIdx.x; c < kc; c += kThreads) {
+    uint4 v[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+      v[t] = t < m ? __ldcg(reinterpret_cast<const uint4*>(xg + (static_cast<size_t>(t) * k + c * 8) * 2))
+                   : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int t = 0; t < MT; ++t) *reinterpret_cast<uint4*>(xs + (static_cast<size_t>(t) * k + c * 8) * 2) = v[t];
+  }
+  __syncthreads();
+  const bool ok = wait_bounded(bar, p.status);
+  if (__syncthreads_and(ok) == 0) {
+    if (threadIdx.x == 0) mbar_wait_time(bar, 0);       // the copy has landed before the CTA exits
+    return;
+  }
+
+  // ---- per warp: rows warp, warp + 8, ...; per lane: K chunks lane, lane + 32, ...
+  unsigned long long acc[kRpw][MT], accu[kRpw][MT];
+#pragma unroll
+  for (int i = 0; i < kRpw; ++i)
+#pragma unroll
+    for (int t = 0; t < MT; ++t) acc[i][t] = accu[i][t] = 0ull;
+  for (int c = lane; c < k / 16; c += 32) {
+    unsigned long long xv[MT][8];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const uint4* xp = reinterpret_cast<const uint4*>(xs + (static_cast<size_t>(t) * k + c * 16) * 2);
+      x8_to_f32x2<XBF16>(xp[0], &xv[t][0]);
+      x8_to_f32x2<XBF16>(xp[1], &xv[t][4]);
+    }
+#pragma unroll
+    for (int i = 0; i < kRpw; ++i) {
+      const int row = warp + kWarps * i;
+      if (row < nr) {
+        unsigned long long w[8];
+        w16_to_f32x2(*reinterpret_cast<const uint4*>(wsm + static_cast<size_t>(row) * k + c * 16), w);
+#pragma unroll
+        for (int t = 0; t < MT; ++t)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ffma2(acc[i][t], w[e], xv[t][e]);
+        if constexpr (SWIGLU) {
+          w16_to_f32x2(*reinterpret_cast<const uint4*>(wsm + (static_cast<size_t>(R) + row) * k + c * 16), w);
+#pragma unroll
+          for (int t = 0; t < MT; ++t)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ffma2(accu[i][t], w[e], xv[t][e]);
+        }
+      }
+    }
+  }
+  // ---- reduce all of the warp's sums at once (transposing butterfly), scale, store
+  constexpr int V = kRpw * MT * H;                       // value (i, t, h) at index (i * MT + t) * H + h
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < kRpw; ++i)
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      v[(i * MT + t) * H] = sum2(acc[i][t]);
+      if constexpr (SWIGLU) v[(i * MT + t) * H + 1] = sum2(accu[i][t]);
+    }
+  const float total = warp_reduce_multi<V>(v);
+  const int idx = value_index_of_lane<V>(lane);          // the value this lane now holds in full
+  constexpr int kLanesPerValue = 32 / V;
+  // the lowest index bit (h) comes from lane bit 5 - log2(V): the up sum of a
+  // SwiGLU pair sits on the lane that differs in that bit
+  constexpr int kHBit = kLanesPerValue;
+  const float up = SWIGLU ? __shfl_xor_sync(0xFFFFFFFFu, total, kHBit) : 0.f;
+  const int i = idx / (MT * H), t = (idx / H) % MT, h = idx % H;
+  const int row = warp + kWarps * i;
+  if (lane % kLanesPerValue == 0 && h == 0 && row < nr && t < m) {
+    const float g = total * sc_sel(sc, i);
+    const float out = SWIGLU ? swiglu_model_ordered<XBF16>(g, up * sc_sel(scu, i)) : g;
+    const int n = r0 + row;
+    const long long yi = y_tr ? static_cast<long long>(n) * ldy + t : static_cast<long long>(t) * ldy + n;
+    store_act<XBF16>(y_ptr, yi, out);
+  }
+}
+
+template <int MT, bool SWIGLU, bool XBF16>
+cudaError_t launch_one(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
+  auto kern = gemv_chain_kernel<MT, SWIGLU, XBF16>;
+  static std::atomic<int> configured[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (configured[dev].load(std::memory_order_acquire) == 0) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvChainMaxSmem)) != cudaSuccess)
+      return e;
+    configured[dev].store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <bool SWIGLU, bool XBF16>
+cudaError_t launch_mt(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
+  return plan.mt == 1 ? launch_one<1, SWIGLU, XBF16>(p, plan, pdl, s) : launch_one<2, SWIGLU, XBF16>(p, plan, pdl, s);
+}
+
+}  // namespace
+
+GemvChainPlan plan_gemv_chain(int m, int n, int k, bool swiglu, int sm_count) {
+  GemvChainPlan c{};
+  c.ok = false;
+  if (m < 1 || m > kGemvChainMaxM || n < 1 || k < 16 || k % 16 || sm_count < 1) return c;
+  if (swiglu && (n % 2)) return c;
+  const int n_out = swiglu ? n / 2 : n;
+  const int h = swiglu ? 2 : 1;
+  c.mt = m <= 1 ? 1 : 2;
+  // about one CTA per SM, at most kRpw rows per warp
+  c.rows = (n_out + sm_count - 1) / sm_count;
+  if (c.rows > kWarps * kRpw) return c;                 // large heads stream through the tcgen05 kernel
+  c.grid = (n_out + c.rows - 1) / c.rows;
+  const size_t need = static_cast<size_t>(h) * c.rows * k + static_cast<size_t>(c.mt) * k * 2 + 16;
+  // at least kGemvChainMinSmem, so that at most two CTAs share an SM: the next
+  // linear's CTAs sit beside this one's, and the one after waits for them
+  c.smem = static_cast<int>(std::max<size_t>(need, kGemvChainMinSmem));
+  if (c.smem > kGemvChainMaxSmem) return c;
+  c.ok = true;
+  return c;
+}
+
+cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
+                              cudaStream_t s) {
+  if (swiglu) return xbf16 ? launch_mt<true, true>(p, plan, pdl, s) : launch_mt<true, false>(p, plan, pdl, s);
+  return xbf16 ? launch_mt<false, true>(p, plan, pdl, s) : launch_mt<false, false>(p, plan, pdl, s);
+}
+
+}  // namespace kl

@@ -123,6 +123,29 @@ ChainPlan plan_chain(int m, int n, int k, bool swiglu, int sm_count);
 cudaError_t launch_chain(const ChainParams& p, const ChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
                          cudaStream_t s);
 
+// ---- dependent-chain decode GEMV on CUDA cores for one or two tokens (kl_gemv_chain.cu)
+constexpr int kGemvChainMaxM = 2;
+constexpr int kGemvChainMinSmem = 80 * 1024;   // at most two CTAs per SM
+constexpr int kGemvChainMaxSmem = 227 * 1024;
+struct GemvChainParams {
+  const int8_t* w;                    // int8 [N, K]
+  const void* scales;                 // bf16 [N]
+  const void* x;                      // [M, K] bf16/f16
+  void* y;
+  long long ldy;
+  int m, k, n, n_out;
+  int rows;                           // output rows per CTA
+  int y_transposed;
+  int* status;
+};
+struct GemvChainPlan {
+  bool ok;
+  int mt, rows, grid, smem;
+};
+GemvChainPlan plan_gemv_chain(int m, int n, int k, bool swiglu, int sm_count);
+cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
+                              cudaStream_t s);
+
 // ---- prefill: int8 row-scale GEMM on CTA pairs (kl_tc_prefill.cu)
 constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel
 struct PfParams {

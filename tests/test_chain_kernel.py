@@ -33,7 +33,7 @@ def oracle(x, q, s, swiglu=False):
     return O.swiglu(O.bf16_round(y)) if swiglu else y
 
 
-def kernel_of(m, n, k, swiglu=False, flags=0):
+def kernel_of(m, n, k, swiglu=False, flags=N.KL_FLAG_FORCE_TC):
     return N.describe_plan(m, n, k, N.KL_W8_ROW, swiglu=swiglu, flags=flags,
                            sm_count=torch.cuda.get_device_properties(0).multi_processor_count)["kernel"]
 
@@ -46,7 +46,7 @@ def test_config1_shapes(m, name):
     assert kernel_of(m, n, k, sw) == 4
     x, p, q, s = make(m, n, k, seed=m)
     ref = oracle(x, q, s, sw)
-    y = kl.quant_linear(x.cuda(), p, swiglu=sw)
+    y = kl.quant_linear(x.cuda(), p, swiglu=sw, path="tc")
     assert_matches_oracle(y, ref, what=f"{name} m={m} chain")
     # the persistent kernel on the same inputs meets the same gate
     yp = kl.quant_linear(x.cuda(), p, swiglu=sw, path="persistent")
@@ -64,7 +64,8 @@ def test_config1_shapes(m, name):
 def test_ragged_shapes(m, n, k, sw):
     assert kernel_of(m, n, k, sw) == 4
     x, p, q, s = make(m, n, k, seed=n + k)
-    assert_matches_oracle(kl.quant_linear(x.cuda(), p, swiglu=sw), oracle(x, q, s, sw), what=f"{m}x{n}x{k} sw={sw}")
+    assert_matches_oracle(kl.quant_linear(x.cuda(), p, swiglu=sw, path="tc"), oracle(x, q, s, sw),
+                          what=f"{m}x{n}x{k} sw={sw}")
 
 
 def test_f16_and_transposed():
@@ -127,4 +128,29 @@ def test_persistent_flag_and_large_problems():
     assert kernel_of(1, 4096, 1024, flags=N.KL_FLAG_PERSISTENT) == 2
     assert kernel_of(1, 151936, 1024) == 2
     assert kernel_of(65, 4096, 1024) == 2
+    assert kernel_of(1, 4096, 1024, flags=0) == 5                 # one token: CUDA-core chain GEMV
     assert N.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("name", list(QWEN))
+def test_cuda_core_chain_gemv(m, name):
+    """One or two tokens: the CUDA-core chain GEMV (kernel 5), full rows per CTA."""
+    n, k = QWEN[name]
+    sw = name == "gate_up"
+    assert kernel_of(m, n, k, sw, flags=0) == 5
+    x, p, q, s = make(m, n, k, seed=40 + m)
+    ref = oracle(x, q, s, sw)
+    assert_matches_oracle(kl.quant_linear(x.cuda(), p, swiglu=sw), ref, what=f"{name} m={m} gemv chain")
+    yt = kl.quant_linear(x.cuda(), p, swiglu=sw, transposed=True)
+    assert_matches_oracle(yt.T, ref, what=f"{name} m={m} gemv chain transposed")
+
+
+@pytest.mark.parametrize("m,n,k,sw,dtype", [(1, 17, 128, False, torch.bfloat16), (2, 1000, 1040, True, torch.bfloat16),
+                                            (1, 3072, 3072, False, torch.float16), (2, 4736, 256, False, torch.float16)])
+def test_cuda_core_chain_gemv_ragged(m, n, k, sw, dtype):
+    assert kernel_of(m, n, k, sw, flags=0) == 5
+    x, p, q, s = make(m, n, k, seed=n, dtype=dtype)
+    y = kl.quant_linear(x.cuda(), p, swiglu=sw)
+    assert y.dtype == dtype
+    assert_matches_oracle(y, oracle(x, q, s, sw), what=f"{m}x{n}x{k}")

@@ -67,6 +67,23 @@ def prefill_tokens(m, n_tiles, sm=148):
     return best
 
 
+def gemv_chain_plan(m, n, k, swiglu=False, sm=148):
+    """Restatement of the host planner of the CUDA-core chain GEMV (one or two
+    tokens): about one CTA per SM with full rows, at most 32 output rows per
+    CTA, shared memory padded to 80 KB so that at most two CTAs share an SM."""
+    if m > 2 or k % 16:
+        return None
+    n_out = n // 2 if swiglu else n
+    rows = -(-n_out // sm)
+    if rows > 32:
+        return None
+    mt = 1 if m <= 1 else 2
+    smem = max((2 if swiglu else 1) * rows * k + mt * k * 2 + 16, 80 * 1024)
+    if smem > 227 * 1024:
+        return None
+    return {"rows": rows, "grid": -(-n_out // rows), "mt": mt, "smem": smem}
+
+
 def chain_plan(m, n, k, swiglu=False, sm=148):
     """Restatement of the host planner of the single-tile cluster kernel: the
     fewest 128-wide K blocks per CTA from 2 to 4 that keep the cluster portable
@@ -93,12 +110,22 @@ def test_plan_partition_w8(kl, m, n, k):
     N = kl._native
     plan = N.describe_plan(m, n, k, N.KL_W8_ROW, sm_count=148)
     chain = chain_plan(m, n, k)
+    gchain = gemv_chain_plan(m, n, k)
     # M >= 256 with K a multiple of 64 runs on the CTA-pair prefill kernel
     if m >= 256 and k % 64 == 0:
         assert plan["kernel"] == 3
         tok = prefill_tokens(m, (n + 255) // 256)
         assert plan["grid"] % 2 == 0 and plan["n_mma"] == tok and 1 <= plan["grid"] <= 148
         assert plan["tiles"] == ((n + 255) // 256) * ((m + tok - 1) // tok)
+    elif gchain is not None:
+        # one or two tokens: full rows per CTA on CUDA cores
+        assert plan["kernel"] == 5
+        assert (plan["grid"], plan["tiles"], plan["n_mma"], plan["smem"]) == \
+            (gchain["grid"], gchain["rows"], gchain["mt"], gchain["smem"])
+        assert plan["grid"] <= 148 and 80 * 1024 <= plan["smem"] <= 227 * 1024   # at most two CTAs per SM
+        # the tcgen05 kernels stay available for the same problem (KL_FLAG_FORCE_TC)
+        forced = N.describe_plan(m, n, k, N.KL_W8_ROW, flags=N.KL_FLAG_FORCE_TC, sm_count=148)
+        assert forced["kernel"] == (4 if chain is not None else 2)
     elif chain is not None:
         # one decode linear small enough for the single-tile cluster kernel
         assert plan["kernel"] == 4
@@ -131,7 +158,7 @@ def test_chain_plan_config1_shapes(kl):
               (1024, 3072, False): (8, 8, 8)}
     for (n, k, sw), (tiles, csize, csize64) in expect.items():
         for m in (1, 8, 32, 64):
-            plan = N.describe_plan(m, n, k, N.KL_W8_ROW, swiglu=sw, sm_count=148)
+            plan = N.describe_plan(m, n, k, N.KL_W8_ROW, swiglu=sw, flags=N.KL_FLAG_FORCE_TC, sm_count=148)
             want = csize64 if m > 32 else csize
             assert plan["kernel"] == 4 and (plan["tiles"], plan["units"]) == (tiles, want), (n, k, m, plan)
     assert N.describe_plan(1, 151936, 1024, N.KL_W8_ROW, sm_count=148)["kernel"] == 2
@@ -145,6 +172,8 @@ def test_plan_partition_swiglu(kl, m, n, k):
         tok = prefill_tokens(m, (n // 2 + 127) // 128)
         assert plan["kernel"] == 3 and plan["n_mma"] == tok
         assert plan["tiles"] == ((n // 2 + 127) // 128) * ((m + tok - 1) // tok)
+    elif gemv_chain_plan(m, n, k, swiglu=True) is not None:
+        assert plan["kernel"] == 5 and plan["tiles"] == gemv_chain_plan(m, n, k, swiglu=True)["rows"]
     elif chain_plan(m, n, k, swiglu=True) is not None:
         assert plan["kernel"] == 4 and plan["tiles"] == (n // 2 + 63) // 64
     else:
