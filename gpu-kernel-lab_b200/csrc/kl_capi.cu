@@ -289,15 +289,18 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     return KL_OK;
   }
 
-  if (tc && w_format == KL_W8_ROW && !(flags & (KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC))) {
+  if (sm100 && !(flags & (KL_FLAG_FORCE_SIMT | KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC)) && aligned16(x) &&
+      aligned16(w) && (w_format == KL_W8_ROW || is_w4(w_format))) {
     // One or two tokens: full rows per CTA on CUDA cores, nothing exchanged
     // between CTAs (the shortest path after the dependency wait)
-    const GemvChainPlan gp = plan_gemv_chain(m, n, k, swiglu != 0, di.sm_count);
+    const GemvChainPlan gp = plan_gemv_chain(m, n, k, w_format, group, swiglu != 0, di.sm_count);
     if (gp.ok) {
       GemvChainParams c;
       std::memset(&c, 0, sizeof(c));
-      c.w = static_cast<const int8_t*>(w);
+      c.w = w;
       c.scales = scales;
+      c.zeros = zeros;
+      c.group = group;
       c.x = x;
       c.y = y;
       c.ldy = transposed ? m : n_out;
@@ -308,7 +311,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
       c.rows = gp.rows;
       c.y_transposed = transposed ? 1 : 0;
       c.status = di.status;
-      const cudaError_t e = launch_gemv_chain(c, gp, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
+      const cudaError_t e = launch_gemv_chain(c, gp, w_format, swiglu != 0, xbf16, (flags & KL_FLAG_PDL) != 0, s);
       if (e != cudaSuccess) return cuda_fail(e, "chain GEMV launch");
       return KL_OK;
     }
@@ -819,8 +822,8 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
       return fail(KL_ERR_INVALID, "pair plan out of range");
     return KL_OK;
   }
-  if (w_format == KL_W8_ROW && !(flags & (KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC))) {
-    const GemvChainPlan gp = plan_gemv_chain(m, n, k, swiglu != 0, sm_count);
+  if ((w_format == KL_W8_ROW || is_w4(w_format)) && !(flags & (KL_FLAG_PERSISTENT | KL_FLAG_FORCE_TC))) {
+    const GemvChainPlan gp = plan_gemv_chain(m, n, k, w_format, group, swiglu != 0, sm_count);
     if (gp.ok) {
       out[0] = 5;
       out[1] = gp.grid;

@@ -2,9 +2,14 @@
 // model forward: every linear waits for the op that produced its input; the
 // call pattern of profiling/decode_stage2_ablation.py:78-143 around the op of
 // learning/10_cuda_decode/warp_gemv.cu:56-90, whose per-row warp GEMV this
-// replaces for the int8 row format).
+// replaces for the int8 row format, and of learning/09_int4/kernels.py:67-75
+// for 4-bit weights).
 //
-//   y[m, n] = scale[n] * sum_k x[m, k] * q[n, k]      (f32 accumulate, bf16/f16 out)
+//   int8 rows:  y[m, n] = scale[n] * sum_k x[m, k] * q[n, k]
+//   4-bit:      y[m, n] = sum_g scale[n, g] * sum_{k in g} x[m, k] * (q[n, k] - zero[n, g])
+//               (asymmetric: bf16 scale and zero per group; symmetric: f32
+//               scale, two's-complement nibbles, i.e. zero 8 after q ^ 8)
+//   f32 accumulate, bf16/f16 out.
 //
 // For one or two tokens the arithmetic is small (4 M multiply-adds for a 4 MB
 // QKV, spread over the SMs) and the time of a dependent linear is latency.
@@ -15,14 +20,17 @@
 //   * Each CTA owns `rows` output rows with all of K (gate and up rows of a
 //     SwiGLU pair together), so nothing is exchanged between CTAs.
 //   * Before the wait: one bulk copy of the CTA's weight rows (contiguous in
-//     the [N, K] layout) into shared memory, and the row scales into registers.
+//     the [N, K] and [N, K/2] layouts) into shared memory; the row scales into
+//     registers, or the group scales and zero points into shared memory.
 //     The dependent kernel is triggered first, so the next linear's CTAs can
 //     start and fetch their weights while this one waits and computes.
 //   * After the wait: the activations (2 KB per token at K = 1024) are staged
 //     in shared memory once; each warp takes its rows, each lane a strided
-//     set of 16-element K chunks: exact int8 -> f32 (the 2^23 magic number),
-//     packed f32x2 multiply-adds against the activations kept in registers
-//     across the warp's rows, one warp reduction per output, scale and store.
+//     set of 16-element K chunks: exact integer -> f32 (the 2^23 magic number;
+//     the zero point folds into the same packed subtract), packed f32x2
+//     multiply-adds against the activations kept in registers across the
+//     warp's rows (4-bit: one chunk lies in one group, whose scale multiplies
+//     the chunk's sum), one transposing warp reduction, scale and store.
 //
 // Every wait is bounded; on expiry the kernel records KL_ERR_TIMEOUT and
 // waits (bounded) for its own copy before returning.
@@ -73,6 +81,25 @@ KL_DEVICE void w16_to_f32x2(const uint4& v, unsigned long long (&w)[8]) {
     w[2 * i + 1] = fsub2(b, bias);
   }
 }
+// 16 nibbles (low nibble = even k) -> 8 f32 pairs (2^23 + c, c the code, with
+// c ^ 8 for two's-complement codes), minus `bias` = (2^23 + zero) in both
+// halves: exactly q - zero.
+template <bool SYM>
+KL_DEVICE void w4x16_to_f32x2(const uint2& v, unsigned long long bias, unsigned long long (&w)[8]) {
+  constexpr uint32_t kFlip = SYM ? 0x08080808u : 0u;
+  const uint32_t wd[2] = {v.x, v.y};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t lo = lop3<0x6A>(wd[i], 0x0F0F0F0Fu, kFlip);          // even-k codes, one per byte
+    const uint32_t hi = lop3<0x6A>(wd[i] >> 4, 0x0F0F0F0Fu, kFlip);     // odd-k codes
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      unsigned long long a;
+      asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "r"(prmt(lo, 0x4B000000u, 0x7540u + j)), "r"(prmt(hi, 0x4B000000u, 0x7540u + j)));
+      w[4 * i + j] = fsub2(a, bias);
+    }
+  }
+}
 // 8 activations (one 16-byte chunk) -> 4 f32 pairs.
 template <bool XBF16>
 KL_DEVICE void x8_to_f32x2(const uint4& v, unsigned long long* out) {
@@ -96,6 +123,21 @@ KL_DEVICE float sc_sel(const float (&s)[kRpw], int i) {
   return r;
 }
 
+// Shared memory: weight rows [H][R][rb], then (4-bit) group scales and zero
+// points [H][R][G] as float pairs, then the activations [MT][K], then the
+// weights' mbarrier.
+struct GemvChainLayout {
+  size_t groups, x, bar, total;
+};
+__host__ __device__ inline GemvChainLayout gemv_chain_layout(int h, int rows, int rb, int groups, int mt, int k) {
+  GemvChainLayout l{};
+  l.groups = static_cast<size_t>(h) * rows * rb;                            // rb is a multiple of 16
+  l.x = l.groups + ((static_cast<size_t>(h) * rows * groups * 8 + 15) & ~static_cast<size_t>(15));
+  l.bar = l.x + static_cast<size_t>(mt) * k * 2;
+  l.total = l.bar + 16;
+  return l;
+}
+
 KL_DEVICE bool wait_bounded(uint32_t bar, int* status) {
   if (mbar_try_wait(bar, 0)) return true;
   const unsigned long long t0 = globaltimer();
@@ -108,37 +150,63 @@ KL_DEVICE bool wait_bounded(uint32_t bar, int* status) {
   }
 }
 
-template <int MT, bool SWIGLU, bool XBF16>
+template <int FMT, int MT, bool SWIGLU, bool XBF16>
 __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_constant__ GemvChainParams p) {
+  constexpr bool W4 = FMT != KL_W8_ROW;
   constexpr int H = SWIGLU ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int k = p.k, R = p.rows;
+  const int rb = W4 ? k / 2 : k;                         // bytes of one weight row
+  const int G = W4 ? k / p.group : 0;                    // groups per row (4-bit)
   const int r0 = blockIdx.x * R;
   const int nr = min(R, p.n_out - r0);                   // output rows of this CTA
-  uint8_t* wsm = smem;                                   // [H][R][K] int8
-  uint8_t* xs = smem + static_cast<size_t>(H) * R * k;   // [MT][K] activations (bf16/f16)
-  const uint32_t bar = smem_u32(xs + static_cast<size_t>(MT) * k * 2);
+  const GemvChainLayout L = gemv_chain_layout(H, R, rb, G, MT, k);
+  uint8_t* wsm = smem;                                   // [H][R][rb] weight rows
+  float2* gsm = reinterpret_cast<float2*>(smem + L.groups);   // [H][R][G] (scale, 2^23 + zero)
+  uint8_t* xs = smem + L.x;                              // [MT][K] activations (bf16/f16)
+  const uint32_t bar = smem_u32(smem + L.bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint8_t* wg = static_cast<const uint8_t*>(p.w);
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
-    const uint32_t bytes = static_cast<uint32_t>(nr) * k;
+    const uint32_t bytes = static_cast<uint32_t>(nr) * rb;
     mbar_arrive_expect_tx(bar, H * bytes);
     // weights are static: fetch them while the previous kernel runs
-    bulk_copy_g2s(smem_u32(wsm), p.w + static_cast<size_t>(r0) * k, bytes, bar);
+    bulk_copy_g2s(smem_u32(wsm), wg + static_cast<size_t>(r0) * rb, bytes, bar);
     if constexpr (SWIGLU)
-      bulk_copy_g2s(smem_u32(wsm + static_cast<size_t>(R) * k), p.w + static_cast<size_t>(p.n_out + r0) * k, bytes,
+      bulk_copy_g2s(smem_u32(wsm + static_cast<size_t>(R) * rb), wg + static_cast<size_t>(p.n_out + r0) * rb, bytes,
                     bar);
   }
   __syncthreads();                                       // barrier initialised before anyone waits on it
   pdl_launch_dependents();
   float sc[kRpw], scu[kRpw];
+  if constexpr (W4) {
+    // group scales and zero points of the CTA's rows (static data, read before the wait)
+    const int per_h = nr * G;
+    for (int e = threadIdx.x; e < H * per_h; e += kThreads) {
+      const int h = e / per_h, rem = e - h * per_h, row = rem / G, g = rem - row * G;
+      const long long gi = static_cast<long long>(h * p.n_out + r0 + row) * G + g;
+      float sv, zv;
+      if constexpr (FMT == KL_W4_ASYM) {
+        sv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.scales)[gi]);
+        zv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.zeros)[gi]);
+      } else {
+        sv = reinterpret_cast<const float*>(p.scales)[gi];
+        zv = 8.0f;                                       // codes flipped by ^ 8 in the conversion
+      }
+      gsm[(h * R + row) * G + g] = make_float2(sv, 8388608.0f + zv);
+    }
 #pragma unroll
-  for (int i = 0; i < kRpw; ++i) {
-    const int row = warp + kWarps * i;
-    const __nv_bfloat16* s = reinterpret_cast<const __nv_bfloat16*>(p.scales);
-    sc[i] = row < nr ? __bfloat162float(s[r0 + row]) : 0.f;
-    scu[i] = (SWIGLU && row < nr) ? __bfloat162float(s[p.n_out + r0 + row]) : 0.f;
+    for (int i = 0; i < kRpw; ++i) sc[i] = scu[i] = 1.0f;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kRpw; ++i) {
+      const int row = warp + kWarps * i;
+      const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(p.scales);
+      sc[i] = row < nr ? __bfloat162float(sp[r0 + row]) : 0.f;
+      scu[i] = (SWIGLU && row < nr) ? __bfloat162float(sp[p.n_out + r0 + row]) : 0.f;
+    }
   }
   void* y_ptr = p.y;
   long long ldy = p.ldy;
@@ -185,22 +253,34 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
       x8_to_f32x2<XBF16>(xp[0], &xv[t][0]);
       x8_to_f32x2<XBF16>(xp[1], &xv[t][4]);
     }
+    const int grp = W4 ? (c * 16) / p.group : 0;        // the chunk's group (4-bit)
 #pragma unroll
     for (int i = 0; i < kRpw; ++i) {
       const int row = warp + kWarps * i;
       if (row < nr) {
-        unsigned long long w[8];
-        w16_to_f32x2(*reinterpret_cast<const uint4*>(wsm + static_cast<size_t>(row) * k + c * 16), w);
 #pragma unroll
-        for (int t = 0; t < MT; ++t)
+        for (int h = 0; h < H; ++h) {
+          unsigned long long w[8];
+          unsigned long long(&a)[MT] = h ? accu[i] : acc[i];
+          const uint8_t* wrow = wsm + (static_cast<size_t>(h) * R + row) * rb;
+          if constexpr (W4) {
+            const float2 sz = gsm[(h * R + row) * G + grp];
+            w4x16_to_f32x2<FMT == KL_W4_SYM>(*reinterpret_cast<const uint2*>(wrow + c * 8), pack2(sz.y, sz.y), w);
+            const unsigned long long s2 = pack2(sz.x, sz.x);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) ffma2(acc[i][t], w[e], xv[t][e]);
-        if constexpr (SWIGLU) {
-          w16_to_f32x2(*reinterpret_cast<const uint4*>(wsm + (static_cast<size_t>(R) + row) * k + c * 16), w);
+            for (int t = 0; t < MT; ++t) {
+              unsigned long long d = 0ull;               // the chunk's sum, then scaled by its group's scale
 #pragma unroll
-          for (int t = 0; t < MT; ++t)
+              for (int e = 0; e < 8; ++e) ffma2(d, w[e], xv[t][e]);
+              ffma2(a[t], d, s2);
+            }
+          } else {
+            w16_to_f32x2(*reinterpret_cast<const uint4*>(wrow + c * 16), w);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ffma2(accu[i][t], w[e], xv[t][e]);
+            for (int t = 0; t < MT; ++t)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ffma2(a[t], w[e], xv[t][e]);
+          }
         }
       }
     }
@@ -233,9 +313,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
   }
 }
 
-template <int MT, bool SWIGLU, bool XBF16>
+template <int FMT, int MT, bool SWIGLU, bool XBF16>
 cudaError_t launch_one(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
-  auto kern = gemv_chain_kernel<MT, SWIGLU, XBF16>;
+  auto kern = gemv_chain_kernel<FMT, MT, SWIGLU, XBF16>;
   static std::atomic<int> configured[kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -259,17 +339,29 @@ cudaError_t launch_one(const GemvChainParams& p, const GemvChainPlan& plan, bool
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <bool SWIGLU, bool XBF16>
+template <int FMT, bool SWIGLU, bool XBF16>
 cudaError_t launch_mt(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
-  return plan.mt == 1 ? launch_one<1, SWIGLU, XBF16>(p, plan, pdl, s) : launch_one<2, SWIGLU, XBF16>(p, plan, pdl, s);
+  return plan.mt == 1 ? launch_one<FMT, 1, SWIGLU, XBF16>(p, plan, pdl, s)
+                      : launch_one<FMT, 2, SWIGLU, XBF16>(p, plan, pdl, s);
+}
+
+template <int FMT>
+cudaError_t launch_fmt(const GemvChainParams& p, const GemvChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
+                       cudaStream_t s) {
+  if (swiglu) return xbf16 ? launch_mt<FMT, true, true>(p, plan, pdl, s) : launch_mt<FMT, true, false>(p, plan, pdl, s);
+  return xbf16 ? launch_mt<FMT, false, true>(p, plan, pdl, s) : launch_mt<FMT, false, false>(p, plan, pdl, s);
 }
 
 }  // namespace
 
-GemvChainPlan plan_gemv_chain(int m, int n, int k, bool swiglu, int sm_count) {
+GemvChainPlan plan_gemv_chain(int m, int n, int k, int w_format, int group, bool swiglu, int sm_count) {
   GemvChainPlan c{};
   c.ok = false;
+  const bool w4 = w_format == KL_W4_ASYM || w_format == KL_W4_SYM;
+  if (!(w_format == KL_W8_ROW || w4)) return c;
   if (m < 1 || m > kGemvChainMaxM || n < 1 || k < 16 || k % 16 || sm_count < 1) return c;
+  // 4-bit: a 16-element chunk lies in one group; rows of K/2 bytes are whole 16-byte units
+  if (w4 && (group < 16 || group % 16 || k % group || k % 32)) return c;
   if (swiglu && (n % 2)) return c;
   const int n_out = swiglu ? n / 2 : n;
   const int h = swiglu ? 2 : 1;
@@ -278,19 +370,23 @@ GemvChainPlan plan_gemv_chain(int m, int n, int k, bool swiglu, int sm_count) {
   c.rows = (n_out + sm_count - 1) / sm_count;
   if (c.rows > kWarps * kRpw) return c;                 // large heads stream through the tcgen05 kernel
   c.grid = (n_out + c.rows - 1) / c.rows;
-  const size_t need = static_cast<size_t>(h) * c.rows * k + static_cast<size_t>(c.mt) * k * 2 + 16;
+  const GemvChainLayout L = gemv_chain_layout(h, c.rows, w4 ? k / 2 : k, w4 ? k / group : 0, c.mt, k);
   // at least kGemvChainMinSmem, so that at most two CTAs share an SM: the next
   // linear's CTAs sit beside this one's, and the one after waits for them
-  c.smem = static_cast<int>(std::max<size_t>(need, kGemvChainMinSmem));
-  if (c.smem > kGemvChainMaxSmem) return c;
+  c.smem = std::max<int>(static_cast<int>(L.total), kGemvChainMinSmem);
+  if (L.total > static_cast<size_t>(kGemvChainMaxSmem)) return c;
   c.ok = true;
   return c;
 }
 
-cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
-                              cudaStream_t s) {
-  if (swiglu) return xbf16 ? launch_mt<true, true>(p, plan, pdl, s) : launch_mt<true, false>(p, plan, pdl, s);
-  return xbf16 ? launch_mt<false, true>(p, plan, pdl, s) : launch_mt<false, false>(p, plan, pdl, s);
+cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, int w_format, bool swiglu,
+                              bool xbf16, bool pdl, cudaStream_t s) {
+  switch (w_format) {
+    case KL_W8_ROW: return launch_fmt<KL_W8_ROW>(p, plan, swiglu, xbf16, pdl, s);
+    case KL_W4_ASYM: return launch_fmt<KL_W4_ASYM>(p, plan, swiglu, xbf16, pdl, s);
+    case KL_W4_SYM: return launch_fmt<KL_W4_SYM>(p, plan, swiglu, xbf16, pdl, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace kl

@@ -128,12 +128,13 @@ constexpr int kGemvChainMaxM = 2;
 constexpr int kGemvChainMinSmem = 80 * 1024;   // at most two CTAs per SM
 constexpr int kGemvChainMaxSmem = 227 * 1024;
 struct GemvChainParams {
-  const int8_t* w;                    // int8 [N, K]
-  const void* scales;                 // bf16 [N]
+  const void* w;                      // int8 [N, K] or packed 4-bit [N, K/2]
+  const void* scales;                 // bf16 [N] (int8 rows); bf16 / f32 [N, K/group] (4-bit)
+  const void* zeros;                  // bf16 [N, K/group] (asymmetric 4-bit), else unused
   const void* x;                      // [M, K] bf16/f16
   void* y;
   long long ldy;
-  int m, k, n, n_out;
+  int m, k, n, n_out, group;
   int rows;                           // output rows per CTA
   int y_transposed;
   int* status;
@@ -142,9 +143,10 @@ struct GemvChainPlan {
   bool ok;
   int mt, rows, grid, smem;
 };
-GemvChainPlan plan_gemv_chain(int m, int n, int k, bool swiglu, int sm_count);
-cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, bool swiglu, bool xbf16, bool pdl,
-                              cudaStream_t s);
+// Formats: KL_W8_ROW, KL_W4_ASYM, KL_W4_SYM (group a multiple of 16 dividing K).
+GemvChainPlan plan_gemv_chain(int m, int n, int k, int w_format, int group, bool swiglu, int sm_count);
+cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& plan, int w_format, bool swiglu,
+                              bool xbf16, bool pdl, cudaStream_t s);
 
 // ---- prefill: int8 row-scale GEMM on CTA pairs (kl_tc_prefill.cu)
 constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel

@@ -154,3 +154,55 @@ def test_cuda_core_chain_gemv_ragged(m, n, k, sw, dtype):
     y = kl.quant_linear(x.cuda(), p, swiglu=sw)
     assert y.dtype == dtype
     assert_matches_oracle(y, oracle(x, q, s, sw), what=f"{m}x{n}x{k}")
+
+
+def make_w4(m, n, k, fmt, group=128, seed=0, dtype=torch.bfloat16):
+    gen = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=gen) * 0.02
+    x = torch.randn(m, k, generator=gen).to(dtype)
+    if fmt == "asym":
+        p = kl.quantize_int4_asym(w.cuda(), group)
+        deq = O.dequantize_int4_asym(p.data.cpu().numpy(), p.scales.float().cpu().numpy(),
+                                     p.zeros.float().cpu().numpy(), group)
+    else:
+        p = kl.quantize_int4(w.cuda(), group)
+        deq = O.dequantize_int4(p.data.cpu().numpy(), p.scales.cpu().numpy(), group)
+    return x, p, deq
+
+
+@pytest.mark.parametrize("fmt", ["asym", "sym"])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("name", list(QWEN))
+def test_cuda_core_chain_gemv_w4(fmt, m, name):
+    """4-bit weights, one or two tokens: the chain GEMV (kernel 5) with the
+    group scale applied per 16-element chunk and the zero point folded into the
+    exact integer conversion."""
+    n, k = QWEN[name]
+    sw = name == "gate_up"
+    f = N.KL_W4_ASYM if fmt == "asym" else N.KL_W4_SYM
+    assert N.describe_plan(m, n, k, f, swiglu=sw, sm_count=torch.cuda.get_device_properties(0).multi_processor_count)["kernel"] == 5
+    x, p, deq = make_w4(m, n, k, fmt, seed=60 + m)
+    ref = O.linear_f32(x.float().numpy(), deq)
+    if sw:
+        ref = O.swiglu(O.bf16_round(ref))
+    y = kl.quant_linear(x.cuda(), p, swiglu=sw)
+    assert_matches_oracle(y, ref, what=f"w4 {fmt} {name} m={m} gemv chain")
+    yt = kl.quant_linear(x.cuda(), p, swiglu=sw, transposed=True)
+    assert_matches_oracle(yt.T, ref, what=f"w4 {fmt} {name} m={m} transposed")
+    # the persistent tcgen05 kernel on the same inputs meets the same gate
+    yp = kl.quant_linear(x.cuda(), p, swiglu=sw, path="persistent")
+    assert_matches_oracle(yp, ref, what=f"w4 {fmt} {name} m={m} persistent")
+
+
+@pytest.mark.parametrize("fmt,m,n,k,group,dtype", [
+    ("sym", 1, 17, 128, 32, torch.bfloat16),      # group 32: four groups per 128 columns
+    ("sym", 2, 1000, 1088, 64, torch.float16),    # group 64, K not a multiple of 128
+    ("asym", 1, 300, 4096, 128, torch.float16),
+    ("asym", 2, 4733, 256, 128, torch.bfloat16),  # 32 rows per CTA, partial last CTA
+])
+def test_cuda_core_chain_gemv_w4_ragged(fmt, m, n, k, group, dtype):
+    x, p, deq = make_w4(m, n, k, fmt, group=group, seed=n, dtype=dtype)
+    y = kl.quant_linear(x.cuda(), p)
+    assert y.dtype == dtype
+    assert_matches_oracle(y, O.linear_f32(x.float().numpy(), deq), what=f"w4 {fmt} {m}x{n}x{k} g{group}")
+    assert N.device_status(0) == 0

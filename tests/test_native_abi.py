@@ -67,21 +67,27 @@ def prefill_tokens(m, n_tiles, sm=148):
     return best
 
 
-def gemv_chain_plan(m, n, k, swiglu=False, sm=148):
+def gemv_chain_plan(m, n, k, swiglu=False, sm=148, w4=False, group=128):
     """Restatement of the host planner of the CUDA-core chain GEMV (one or two
     tokens): about one CTA per SM with full rows, at most 32 output rows per
-    CTA, shared memory padded to 80 KB so that at most two CTAs share an SM."""
+    CTA, shared memory padded to 80 KB so that at most two CTAs share an SM.
+    4-bit rows take K/2 bytes plus an 8-byte (scale, zero) pair per group, and
+    need a group that is a multiple of 16 dividing K, and K % 32 == 0."""
     if m > 2 or k % 16:
+        return None
+    if w4 and (group % 16 or k % group or k % 32):
         return None
     n_out = n // 2 if swiglu else n
     rows = -(-n_out // sm)
     if rows > 32:
         return None
     mt = 1 if m <= 1 else 2
-    smem = max((2 if swiglu else 1) * rows * k + mt * k * 2 + 16, 80 * 1024)
-    if smem > 227 * 1024:
+    h = 2 if swiglu else 1
+    groups = h * rows * (k // group) * 8 if w4 else 0
+    need = h * rows * (k // 2 if w4 else k) + ((groups + 15) // 16) * 16 + mt * k * 2 + 16
+    if need > 227 * 1024:
         return None
-    return {"rows": rows, "grid": -(-n_out // rows), "mt": mt, "smem": smem}
+    return {"rows": rows, "grid": -(-n_out // rows), "mt": mt, "smem": max(need, 80 * 1024)}
 
 
 def chain_plan(m, n, k, swiglu=False, sm=148):
@@ -180,11 +186,20 @@ def test_plan_partition_swiglu(kl, m, n, k):
         assert plan["kernel"] == 2 and plan["tiles"] == ((n // 2 + 63) // 64) * ((m + plan["n_mma"] - 1) // plan["n_mma"])
 
 
-@pytest.mark.parametrize("m", [1, 16, 200])
+@pytest.mark.parametrize("m", [1, 2, 16, 200])
 @pytest.mark.parametrize("n,k", QWEN)
 def test_plan_partition_w4(kl, m, n, k):
-    plan = kl._native.describe_plan(m, n, k, kl._native.KL_W4_ASYM, sm_count=148)
-    assert plan["kernel"] == 2 and plan["n_mma"] <= 64
+    N = kl._native
+    for fmt in (N.KL_W4_ASYM, N.KL_W4_SYM):
+        plan = N.describe_plan(m, n, k, fmt, sm_count=148)
+        g = gemv_chain_plan(m, n, k, w4=True)
+        if g is not None:
+            # one or two tokens: the CUDA-core chain GEMV with full 4-bit rows
+            assert plan["kernel"] == 5
+            assert (plan["grid"], plan["tiles"], plan["n_mma"], plan["smem"]) == (g["grid"], g["rows"], g["mt"], g["smem"])
+            assert N.describe_plan(m, n, k, fmt, flags=N.KL_FLAG_PERSISTENT, sm_count=148)["kernel"] == 2
+        else:
+            assert plan["kernel"] == 2 and plan["n_mma"] <= 64
 
 
 def test_plan_w4_two_group_stages(kl):
