@@ -684,9 +684,10 @@ def section_config0(kl, device, hbm, dist):
     y = torch.empty(1, n, device=device, dtype=torch.bfloat16)
     nbytes = n * k + 2 * n + 2 * k + 2 * n
     out = {"shape": [1, n, k], "bytes_per_call": nbytes, "l2": f"{copies} weight copies cycled ({copies * n * k >> 20} MiB)"}
-    kernel_names = {None: "single-tile cluster tcgen05 (kl_tc_chain)", "persistent": "stream-K tcgen05 (tc_qgemm)",
+    kernel_names = {None: "CUDA-core chain GEMV, full rows per CTA (kl_gemv_chain)",
+                    "tc": "single-tile cluster tcgen05 (kl_tc_chain)", "persistent": "stream-K tcgen05 (tc_qgemm)",
                     "simt": "CUDA-core GEMV (gemv_vec)"}
-    for path in (None, "persistent", "simt"):
+    for path in (None, "tc", "persistent", "simt"):
         def run(path=path):
             for w in ws:
                 kl.quant_linear(x, w, out=y, pdl=True, path=path)

@@ -830,11 +830,12 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
       out[2] = 256;
       out[3] = gp.smem;
       out[4] = gp.mt;
-      out[5] = 1;
+      out[5] = gp.rpw;
       out[6] = gp.rows;
       out[7] = gp.grid;
       const int n_out = swiglu ? n / 2 : n;
-      if (gp.grid * gp.rows < n_out || (gp.grid - 1) * gp.rows >= n_out || gp.rows > 32 || gp.smem > 227 * 1024)
+      if (gp.grid * gp.rows < n_out || (gp.grid - 1) * gp.rows >= n_out || gp.rows > 8 * gp.rpw ||
+          gp.smem > 227 * 1024)
         return fail(KL_ERR_INVALID, "chain GEMV plan out of range");
       return KL_OK;
     }

@@ -46,7 +46,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRpw = 4;                          // output rows per warp (at most)
+constexpr int kMaxRpw = 8;                       // output rows per warp (at most): 4, or 8 for wide problems
 
 KL_DEVICE unsigned long long pack2(float lo, float hi) {
   unsigned long long r;
@@ -115,11 +115,12 @@ KL_DEVICE void x8_to_f32x2(const uint4& v, unsigned long long* out) {
   }
 }
 
-// s[i] for a runtime i < kRpw without indexing the register array dynamically.
-KL_DEVICE float sc_sel(const float (&s)[kRpw], int i) {
+// s[i] for a runtime i < RPW without indexing the register array dynamically.
+template <int RPW>
+KL_DEVICE float sc_sel(const float (&s)[RPW], int i) {
   float r = s[0];
 #pragma unroll
-  for (int j = 1; j < kRpw; ++j) r = i == j ? s[j] : r;
+  for (int j = 1; j < RPW; ++j) r = i == j ? s[j] : r;
   return r;
 }
 
@@ -150,7 +151,7 @@ KL_DEVICE bool wait_bounded(uint32_t bar, int* status) {
   }
 }
 
-template <int FMT, int MT, bool SWIGLU, bool XBF16>
+template <int FMT, int MT, int kRpw, bool SWIGLU, bool XBF16>
 __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_constant__ GemvChainParams p) {
   constexpr bool W4 = FMT != KL_W8_ROW;
   constexpr int H = SWIGLU ? 2 : 1;
@@ -313,9 +314,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
   }
 }
 
-template <int FMT, int MT, bool SWIGLU, bool XBF16>
+template <int FMT, int MT, int RPW, bool SWIGLU, bool XBF16>
 cudaError_t launch_one(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
-  auto kern = gemv_chain_kernel<FMT, MT, SWIGLU, XBF16>;
+  auto kern = gemv_chain_kernel<FMT, MT, RPW, SWIGLU, XBF16>;
   static std::atomic<int> configured[kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -341,8 +342,12 @@ cudaError_t launch_one(const GemvChainParams& p, const GemvChainPlan& plan, bool
 
 template <int FMT, bool SWIGLU, bool XBF16>
 cudaError_t launch_mt(const GemvChainParams& p, const GemvChainPlan& plan, bool pdl, cudaStream_t s) {
-  return plan.mt == 1 ? launch_one<FMT, 1, SWIGLU, XBF16>(p, plan, pdl, s)
-                      : launch_one<FMT, 2, SWIGLU, XBF16>(p, plan, pdl, s);
+  if (plan.rpw == 4)
+    return plan.mt == 1 ? launch_one<FMT, 1, 4, SWIGLU, XBF16>(p, plan, pdl, s)
+                        : launch_one<FMT, 2, 4, SWIGLU, XBF16>(p, plan, pdl, s);
+  if (plan.mt == 1) return launch_one<FMT, 1, 8, SWIGLU, XBF16>(p, plan, pdl, s);
+  if constexpr (!SWIGLU) return launch_one<FMT, 2, 8, SWIGLU, XBF16>(p, plan, pdl, s);
+  return cudaErrorInvalidConfiguration;                  // not planned: it would spill registers
 }
 
 template <int FMT>
@@ -366,9 +371,11 @@ GemvChainPlan plan_gemv_chain(int m, int n, int k, int w_format, int group, bool
   const int n_out = swiglu ? n / 2 : n;
   const int h = swiglu ? 2 : 1;
   c.mt = m <= 1 ? 1 : 2;
-  // about one CTA per SM, at most kRpw rows per warp
+  // about one CTA per SM, at most 4 (else 8) rows per warp
   c.rows = (n_out + sm_count - 1) / sm_count;
-  if (c.rows > kWarps * kRpw) return c;                 // large heads stream through the tcgen05 kernel
+  if (c.rows > kWarps * kMaxRpw) return c;              // large heads stream through the tcgen05 kernel
+  c.rpw = c.rows <= kWarps * 4 ? 4 : 8;
+  if (c.rpw == 8 && swiglu && c.mt == 2) return c;      // 32 sums per lane: more registers than a lane has
   c.grid = (n_out + c.rows - 1) / c.rows;
   const GemvChainLayout L = gemv_chain_layout(h, c.rows, w4 ? k / 2 : k, w4 ? k / group : 0, c.mt, k);
   // at least kGemvChainMinSmem, so that at most two CTAs share an SM: the next

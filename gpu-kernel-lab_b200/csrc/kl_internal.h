@@ -142,6 +142,7 @@ struct GemvChainParams {
 struct GemvChainPlan {
   bool ok;
   int mt, rows, grid, smem;
+  int rpw;                            // output rows per warp (4, or 8 above 32 rows per CTA)
 };
 // Formats: KL_W8_ROW, KL_W4_ASYM, KL_W4_SYM (group a multiple of 16 dividing K).
 GemvChainPlan plan_gemv_chain(int m, int n, int k, int w_format, int group, bool swiglu, int sm_count);

@@ -271,8 +271,9 @@ int kl_rmsnorm(const void* x, const void* residual, const void* weight, int dtyp
  * 2 = tcgen05 stream-K GEMM, 3 = tcgen05 CTA-pair prefill GEMM (int8 row scale, M >= 256),
  * 4 = tcgen05 single-tile cluster GEMM for dependent chains (int8 row scale, M <= 64;
  * there stages = K blocks of 128 per CTA and units = CTAs per cluster),
- * 5 = CUDA-core GEMV for dependent chains (int8 row scale, M <= 2; there n_mma =
- * tokens per pass, tiles = output rows per CTA, units = CTAs).
+ * 5 = CUDA-core GEMV for dependent chains (int8 row scale or 4-bit groups of 128
+ * as described here, M <= 2; there n_mma = tokens per pass, stages = output rows
+ * per warp, tiles = output rows per CTA, units = CTAs).
  * KL_FLAG_FORCE_TC keeps kernels 2-4 (tcgen05) for problems kernel 5 would take.
  */
 int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags,

@@ -206,3 +206,28 @@ def test_cuda_core_chain_gemv_w4_ragged(fmt, m, n, k, group, dtype):
     assert y.dtype == dtype
     assert_matches_oracle(y, O.linear_f32(x.float().numpy(), deq), what=f"w4 {fmt} {m}x{n}x{k} g{group}")
     assert N.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,n,k,sw,fmt", [
+    (1, 6144, 1024, False, "w8"),     # gate_up without SwiGLU: 42 rows per CTA, 8 rows per warp
+    (2, 6144, 1024, False, "w8"),
+    (1, 5120, 3072, False, "w8"),     # Llama-3.2-3B fused QKV: 35 rows per CTA
+    (1, 12288, 1024, True, "w8"),     # SwiGLU pair with 42 gate rows per CTA
+    (1, 6144, 1024, False, "asym"),
+    (2, 9472, 512, False, "sym"),     # 64 rows per CTA, the most the kernel takes
+])
+def test_cuda_core_chain_gemv_eight_rows_per_warp(m, n, k, sw, fmt):
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    f = {"w8": N.KL_W8_ROW, "asym": N.KL_W4_ASYM, "sym": N.KL_W4_SYM}[fmt]
+    plan = N.describe_plan(m, n, k, f, swiglu=sw, sm_count=sm)
+    assert plan["kernel"] == 5 and plan["stages"] == (8 if plan["tiles"] > 32 else 4)
+    if fmt == "w8":
+        x, p, q, s = make(m, n, k, seed=n + m)
+        ref = oracle(x, q, s, sw)
+    else:
+        x, p, deq = make_w4(m, n, k, fmt, seed=n + m)
+        ref = O.linear_f32(x.float().numpy(), deq)
+    assert_matches_oracle(kl.quant_linear(x.cuda(), p, swiglu=sw), ref, what=f"{fmt} {m}x{n}x{k} sw={sw}")
+    assert N.device_status(0) == 0
+    # two-token SwiGLU above 32 rows per CTA stays on the tcgen05 chain kernel
+    assert kernel_of(2, 12288, 1024, True, flags=0) == 4

@@ -69,7 +69,7 @@ def prefill_tokens(m, n_tiles, sm=148):
 
 def gemv_chain_plan(m, n, k, swiglu=False, sm=148, w4=False, group=128):
     """Restatement of the host planner of the CUDA-core chain GEMV (one or two
-    tokens): about one CTA per SM with full rows, at most 32 output rows per
+    tokens): about one CTA per SM with full rows, at most 64 output rows per
     CTA, shared memory padded to 80 KB so that at most two CTAs share an SM.
     4-bit rows take K/2 bytes plus an 8-byte (scale, zero) pair per group, and
     need a group that is a multiple of 16 dividing K, and K % 32 == 0."""
@@ -79,15 +79,17 @@ def gemv_chain_plan(m, n, k, swiglu=False, sm=148, w4=False, group=128):
         return None
     n_out = n // 2 if swiglu else n
     rows = -(-n_out // sm)
-    if rows > 32:
-        return None
     mt = 1 if m <= 1 else 2
+    # 4 rows per warp, or 8 above 32 rows per CTA (not for two-token SwiGLU)
+    if rows > 64 or (rows > 32 and swiglu and mt == 2):
+        return None
     h = 2 if swiglu else 1
     groups = h * rows * (k // group) * 8 if w4 else 0
     need = h * rows * (k // 2 if w4 else k) + ((groups + 15) // 16) * 16 + mt * k * 2 + 16
     if need > 227 * 1024:
         return None
-    return {"rows": rows, "grid": -(-n_out // rows), "mt": mt, "smem": max(need, 80 * 1024)}
+    return {"rows": rows, "grid": -(-n_out // rows), "mt": mt, "smem": max(need, 80 * 1024),
+            "rpw": 4 if rows <= 32 else 8}
 
 
 def chain_plan(m, n, k, swiglu=False, sm=148):
@@ -126,8 +128,8 @@ def test_plan_partition_w8(kl, m, n, k):
     elif gchain is not None:
         # one or two tokens: full rows per CTA on CUDA cores
         assert plan["kernel"] == 5
-        assert (plan["grid"], plan["tiles"], plan["n_mma"], plan["smem"]) == \
-            (gchain["grid"], gchain["rows"], gchain["mt"], gchain["smem"])
+        assert (plan["grid"], plan["tiles"], plan["n_mma"], plan["smem"], plan["stages"]) == \
+            (gchain["grid"], gchain["rows"], gchain["mt"], gchain["smem"], gchain["rpw"])
         assert plan["grid"] <= 148 and 80 * 1024 <= plan["smem"] <= 227 * 1024   # at most two CTAs per SM
         # the tcgen05 kernels stay available for the same problem (KL_FLAG_FORCE_TC)
         forced = N.describe_plan(m, n, k, N.KL_W8_ROW, flags=N.KL_FLAG_FORCE_TC, sm_count=148)
