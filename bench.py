@@ -447,8 +447,10 @@ class DecodeSet:
 
 def sharded_head_section(kl, full, ms_list, x_of, world, rank, device, dist, steps, fmt="w8_row"):
     """Vocab-sharded lm_head: the shard GEMM + NCCL all-gather of the logits, and
-    the top-8 alternative (shard GEMM, local top-8, all-gather of candidates,
-    merge), each captured once and replayed; max over ranks."""
+    the top-8 alternative (shard GEMM with the candidates selected in its
+    epilogue, all-gather of candidates, merge), each captured once and replayed;
+    max over ranks.  Beside them, the same two on the whole head on one GPU
+    (every rank runs it alone, no collective), the single-GPU time to beat."""
     import torch
     vocab = full.shape[0]
     lo, hi = kl.sharded_head.shard_bounds(vocab, world, rank)
@@ -483,9 +485,21 @@ def sharded_head_section(kl, full, ms_list, x_of, world, rank, device, dist, ste
         dist.barrier()
         tk = max_over_ranks(timed(tg, reps), dist if world > 1 else None, device)
         del tg
+        logits = torch.empty(m, vocab, dtype=torch.bfloat16, device=device)
+        for _ in range(3):
+            kl.quant_linear(x, full, out=logits)
+            kl.lm_head_topk(x, full, 8)
+        torch.cuda.synchronize()
+        ug = capture(lambda: kl.quant_linear(x, full, out=logits))
+        tu = max_over_ranks(timed(ug, reps), dist if world > 1 else None, device)
+        del ug
+        ugk = capture(lambda: kl.lm_head_topk(x, full, 8))
+        tuk = max_over_ranks(timed(ugk, reps), dist if world > 1 else None, device)
+        del ugk, logits
         res["per_m"][str(m)] = {"ms": round(t, 4), "allgather_bytes": vocab * m * 2,
                                 "shard_weight_GB/s": round(shard.storage_bytes / (t * 1e-3) / 1e9, 1),
-                                "top8_ms": round(tk, 4), "top8_gather_bytes": world * m * 8 * 8}
+                                "top8_ms": round(tk, 4), "top8_gather_bytes": world * m * 8 * 8,
+                                "one_gpu_ms": round(tu, 4), "one_gpu_top8_ms": round(tuk, 4)}
     return res
 
 

@@ -39,6 +39,7 @@
 #include "kl_internal.h"
 
 #include <atomic>
+#include <type_traits>
 
 namespace kl {
 
@@ -245,38 +246,46 @@ struct Cursor {
   }
 };
 
-// 64-bit sort key of a candidate: order-preserving bits of the value rounded
-// to the output type (the selection compares the logits the layer would
-// output), then the inverted row, so that a larger key is the larger value
-// and, on ties, the lower index.  Key 0 is below every real candidate.
-KL_DEVICE unsigned long long topk_key(float v, int row) {
-  const uint32_t u = __float_as_uint(v);
+// 32-bit sort key of a candidate within a 128-row tile: the order-preserving
+// bits of the value rounded to bf16 (the logit the layer would output; zero of
+// either sign as +0) in the high half, the inverted row within the tile in the
+// low half.  A larger key is the larger value and, on ties, the lower row; the
+// value is exact in the key because a bf16 value has 16 bits.  Key 0 is below
+// every real candidate.
+KL_DEVICE uint32_t topk_key(float v_bf16, int row_in_tile) {
+  uint32_t u = __float_as_uint(v_bf16);
+  if ((u & 0x7FFFFFFFu) == 0u) u = 0u;
   const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
+  return (ord & 0xFFFF0000u) | (0xFFFFu - static_cast<uint32_t>(row_in_tile));
 }
 // The merge kernel's packed form: (index << 32) | f32 value bits.
-KL_DEVICE unsigned long long topk_packed(unsigned long long key, long long index_offset) {
-  if (key == 0ull) return (0x7FFFFFFFull << 32) | __float_as_uint(-INFINITY);   // no candidate
-  const uint32_t ord = static_cast<uint32_t>(key >> 32);
-  const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
-  const long long row = static_cast<long long>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+KL_DEVICE unsigned long long topk_packed(uint32_t key, int row0, long long index_offset) {
+  if (key == 0u) return (0x7FFFFFFFull << 32) | __float_as_uint(-INFINITY);   // no candidate
+  const uint32_t ord = key & 0xFFFF0000u;
+  const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFF0000u) : (~ord & 0xFFFF0000u);
+  const long long row = row0 + static_cast<long long>(0xFFFFu - (key & 0xFFFFu));
   return (static_cast<unsigned long long>(row + index_offset) << 32) | u;
 }
-// Bitonic sort of one key per lane across the warp, descending (lane 0 holds the largest).
-KL_DEVICE unsigned long long warp_sort_desc(unsigned long long key) {
+// Bitonic sorts of J independent keys per lane across the warp, descending
+// (lane 0 holds the largest of each).  The J networks run stage by stage side
+// by side, so their shuffles overlap instead of each sort waiting out fifteen
+// dependent shuffle round trips.
+template <int J>
+KL_DEVICE void warp_sort_desc(uint32_t (&key)[J]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
       const bool desc = size == 32 || (lane & size) == 0;
-      const bool lower = (lane & stride) == 0;
-      const bool keep_max = lower == desc;
-      key = keep_max ? (key > other ? key : other) : (key < other ? key : other);
+      const bool keep_max = ((lane & stride) == 0) == desc;
+      uint32_t other[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) other[j] = __shfl_xor_sync(0xFFFFFFFFu, key[j], stride);
+#pragma unroll
+      for (int j = 0; j < J; ++j) key[j] = keep_max ? max(key[j], other[j]) : min(key[j], other[j]);
     }
   }
-  return key;
 }
 
 template <int FMT, int NMMA, int EPI, bool XBF16>
@@ -302,26 +311,60 @@ struct Epi {
     const int m0 = mt * NMMA + cb * 16;
     if constexpr (TOPK) {
       // per token, the tile's top-k rows: each warp sorts its 32 rows, then the
-      // group's first warp merges the four warps' best (all 128 threads call this)
+      // four warps merge the four warps' best, warp w taking tokens w, w + 4, ...
+      // (all 128 threads call this)
+      static_assert(XBF16, "the top-k epilogue keys bf16 logits");
       const int n = nt * 128 + r;
       const bool valid = n < pr.n_out;
       const int lane = r & 31, wq = r >> 5, kk = pr.topk;
-      unsigned long long* xk = reinterpret_cast<unsigned long long*>(xch);   // [4 warps][16 tokens][8]
+      uint32_t* xk = reinterpret_cast<uint32_t*>(xch);   // [4 warps][16 tokens][8]
+      const int mv = pr.m - m0;                          // tokens of these 16 that exist
+      // sorts of tokens j0 .. j0 + J - 1 side by side (as many as exist, rounded up)
+      auto sort_rows = [&](auto jc, auto j0c) {
+        constexpr int J = decltype(jc)::value, j0 = decltype(j0c)::value;   // compile time: v[] stays in registers
+        uint32_t key[J];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (m0 + j < pr.m) {
-          const unsigned long long key = warp_sort_desc(valid ? topk_key(round_act<XBF16>(v[j]), n) : 0ull);
-          if (lane < kk) xk[(wq * 16 + j) * 8 + lane] = key;
-        }
+        for (int jj = 0; jj < J; ++jj)
+          key[jj] = (valid && j0 + jj < mv) ? topk_key(round_act<XBF16>(v[j0 + jj]), r) : 0u;
+        warp_sort_desc<J>(key);
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj)
+          if (j0 + jj < mv && lane < kk) xk[(wq * 16 + j0 + jj) * 8 + lane] = key[jj];
+      };
+      using C0 = std::integral_constant<int, 0>;
+      using C8 = std::integral_constant<int, 8>;
+      if (NMMA == 16 && mv <= 1) {            // the narrow forms only where M <= 16 makes them common
+        sort_rows(std::integral_constant<int, 1>{}, C0{});
+      } else if (NMMA == 16 && mv <= 4) {
+        sort_rows(std::integral_constant<int, 4>{}, C0{});
+      } else {
+        sort_rows(C8{}, C0{});
+        if (mv > 8) sort_rows(C8{}, C8{});
       }
       named_bar_epi(g);
-      if (wq == 0) {
-#pragma unroll 1
-        for (int j = 0; j < 16 && m0 + j < pr.m; ++j) {
-          const unsigned long long key = warp_sort_desc(lane < 4 * kk ? xk[((lane / kk) * 16 + j) * 8 + lane % kk] : 0ull);
-          if (lane < kk)
-            pr.cand[static_cast<long long>(m0 + j) * pr.cand_ld + nt * kk + lane] = topk_packed(key, pr.index_offset);
+      // the four warps merge the four warps' best: warp wq takes tokens wq, wq + 4, ...;
+      // lane l reads candidate l % kk of warp l / kk
+      auto merge_rows = [&](auto tc) {
+        constexpr int T = decltype(tc)::value;
+        const int src = lane < 4 * kk ? (lane / kk) * 16 * 8 + lane % kk : 0;
+        uint32_t key[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int j = wq + 4 * t;
+          key[t] = (j < mv && lane < 4 * kk) ? xk[src + j * 8] : 0u;
         }
+        warp_sort_desc<T>(key);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int j = wq + 4 * t;
+          if (j < mv && lane < kk)
+            pr.cand[static_cast<long long>(m0 + j) * pr.cand_ld + nt * kk + lane] =
+                topk_packed(key[t], nt * 128, pr.index_offset);
+        }
+      };
+      if (wq < mv) {
+        if (NMMA == 16 && mv <= 4) merge_rows(std::integral_constant<int, 1>{});
+        else merge_rows(std::integral_constant<int, 4>{});
       }
       named_bar_epi(g);
       return;
