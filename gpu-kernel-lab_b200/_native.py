@@ -20,6 +20,7 @@ KL_OK, KL_ERR_INVALID, KL_ERR_UNSUPPORTED, KL_ERR_CUDA, KL_ERR_WORKSPACE, KL_ERR
 KL_DT_BF16, KL_DT_F16, KL_DT_F32 = 0, 1, 2
 KL_W8_ROW, KL_W8_GROUP, KL_W4_SYM, KL_W4_ASYM, KL_BF16_DENSE = range(5)
 KL_FLAG_FORCE_SIMT, KL_FLAG_FORCE_TC, KL_FLAG_PDL, KL_FLAG_Y_TRANSPOSED, KL_FLAG_PERSISTENT = 1, 2, 4, 8, 16
+KL_GROUPED_INT8_MMA = 1
 
 EXPORTED_SYMBOLS = (
     "kl_linear", "kl_linear_workspace_bytes", "kl_project", "kl_int4_gemv",
@@ -28,7 +29,7 @@ EXPORTED_SYMBOLS = (
     "kl_device_status", "kl_version", "kl_describe_plan",
     "kl_grouped_table_bytes", "kl_grouped_encode", "kl_grouped_workspace_bytes", "kl_linear_grouped",
     "kl_linear_noalloc", "kl_topk_rows_workspace_bytes", "kl_topk_rows", "kl_topk_merge_rows", "kl_rmsnorm",
-    "kl_linear_topk", "kl_linear_topk_workspace_bytes",
+    "kl_linear_topk", "kl_linear_topk_workspace_bytes", "kl_grouped_digits_bytes", "kl_grouped_encode_ex",
 )
 
 
@@ -57,6 +58,8 @@ _SIGNATURES = {
     "kl_grouped_table_bytes": (_S, [_I]),
     "kl_grouped_encode": (_I, [_P, _I, _I, _I, _I, _P, _S]),
     "kl_grouped_workspace_bytes": (_S, [_P]),
+    "kl_grouped_digits_bytes": (_S, [_P, _I, _I]),
+    "kl_grouped_encode_ex": (_I, [_P, _I, _I, _I, _I, _I, _P, _S, _P, _S]),
     "kl_linear_grouped": (_I, [_P, _P, _P, _S, _I, _P]),
     "kl_linear_noalloc": (_I, [_P, _I, _I, _I, _P, _I, _P, _I, _P, _P]),
     "kl_topk_rows_workspace_bytes": (_S, [_I, _I, _I]),

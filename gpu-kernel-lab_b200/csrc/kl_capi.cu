@@ -409,7 +409,9 @@ struct GroupHeader {
   int n_mma, w_format, swiglu, x_dtype;
   long long units;
   int kblk;
-  uint8_t pad[256 - 36];
+  int int8_mma;                     // 1: KL_GROUPED_INT8_MMA (digits pass + kind::i8 GEMM)
+  int rows_max;                     // int8 mode: largest m_tiles * T of the problems
+  uint8_t pad[256 - 44];
 };
 static_assert(sizeof(GroupHeader) == 256, "group header");
 constexpr uint32_t kGroupMagic = 0x4B4C4752u;   // "KLGR"
@@ -420,9 +422,50 @@ size_t kl_grouped_table_bytes(int count) {
   return sizeof(GroupHeader) + static_cast<size_t>(count) * sizeof(TcProblem);
 }
 
+// Digits area of one problem in the int8 mode: [m_tiles][i8_tile_rows(T)][K]
+// int8, then m_tiles * T f32 token scales, each piece 256-byte aligned.
+static size_t digits_plane_bytes(int m, int k, int tok) {
+  const size_t tiles = static_cast<size_t>((m + tok - 1) / tok);
+  return (tiles * i8_tile_rows(tok) * static_cast<size_t>(k) + 255) & ~static_cast<size_t>(255);
+}
+static size_t digits_scale_bytes(int m, int tok) {
+  const size_t tiles = static_cast<size_t>((m + tok - 1) / tok);
+  return (tiles * tok * sizeof(float) + 255) & ~static_cast<size_t>(255);
+}
+
+size_t kl_grouped_digits_bytes(const kl_problem* problems, int count, int flags) {
+  if (!problems || count <= 0 || count > kMaxGroup || !(flags & KL_GROUPED_INT8_MMA)) return 0;
+  int max_m = 0;
+  for (int i = 0; i < count; ++i) max_m = std::max(max_m, problems[i].m);
+  if (max_m <= 0) return 0;
+  const int tok = tc_choose_tokens_i8(max_m);
+  size_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    if (problems[i].m <= 0 || problems[i].k <= 0) return 0;
+    total += digits_plane_bytes(problems[i].m, problems[i].k, tok) + digits_scale_bytes(problems[i].m, tok);
+  }
+  return total;
+}
+
 int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_format, int swiglu, void* host_table,
                       size_t table_bytes) {
+  return kl_grouped_encode_ex(problems, count, x_dtype, w_format, swiglu, 0, nullptr, 0, host_table, table_bytes);
+}
+
+int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int w_format, int swiglu, int flags,
+                         void* digits, size_t digits_bytes, void* host_table, size_t table_bytes) {
   if (!problems || !host_table) return fail(KL_ERR_INVALID, "problems and host_table must be non-null");
+  if (flags & ~KL_GROUPED_INT8_MMA) return fail(KL_ERR_INVALID, "unknown grouped flags 0x%x", flags);
+  const bool i8 = (flags & KL_GROUPED_INT8_MMA) != 0;
+  if (i8) {
+    if (w_format != KL_W8_ROW || x_dtype != KL_DT_BF16)
+      return fail(KL_ERR_UNSUPPORTED, "the int8-MMA mode takes KL_W8_ROW weights and bf16 activations");
+    if (!digits || (reinterpret_cast<uintptr_t>(digits) & 255u))
+      return fail(KL_ERR_INVALID, "the int8-MMA mode needs a 256-byte-aligned digits buffer");
+    const size_t need = kl_grouped_digits_bytes(problems, count, flags);
+    if (need == 0 || digits_bytes < need)
+      return fail(KL_ERR_WORKSPACE, "digits buffer of %zu bytes required, %zu given", need, digits_bytes);
+  }
   if (count <= 0 || count > kMaxGroup) return fail(KL_ERR_INVALID, "count must be in [1, %d]", kMaxGroup);
   if (table_bytes < kl_grouped_table_bytes(count)) return fail(KL_ERR_INVALID, "host table too small");
   if (!(w_format == KL_W8_ROW || is_w4(w_format)))
@@ -443,7 +486,8 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
   std::memset(hd, 0, sizeof(*hd));
   hd->magic = kGroupMagic;
   hd->count = static_cast<uint32_t>(count);
-  hd->n_mma = tc_choose_nmma(max_m, w_format);
+  hd->n_mma = i8 ? tc_choose_tokens_i8(max_m) : tc_choose_nmma(max_m, w_format);
+  hd->int8_mma = i8 ? 1 : 0;
   hd->w_format = w_format;
   hd->swiglu = swiglu ? 1 : 0;
   hd->x_dtype = x_dtype;
@@ -456,7 +500,7 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
   long long units256 = 0;
   for (int i = 0; i < count; ++i)
     units256 += problem_units(problems[i].m, problems[i].n, problems[i].k, hd->n_mma, 256, swiglu != 0);
-  hd->kblk = tc_choose_kblk(w_format, hd->n_mma, units256, sm);
+  hd->kblk = tc_choose_kblk(i8 ? kFmtI8 : w_format, hd->n_mma, units256, sm);
   if (hd->kblk == 256 && is_w4(w_format)) {   // two 128-groups per stage: every problem must qualify
     for (int i = 0; i < count; ++i)
       if (!two_group_ok(w_format, problems[i].k, problems[i].zeros)) hd->kblk = 128;
@@ -466,8 +510,26 @@ int kl_grouped_encode(const kl_problem* problems, int count, int x_dtype, int w_
     const kl_problem& q = problems[i];
     const int n_out = swiglu ? q.n / 2 : q.n;
     int rc = build_problem(tab[i], q.x, x_dtype, q.m, q.k, q.w, w_format, q.n, q.scales, q.zeros, swiglu, q.y, false,
-                           n_out, hd->n_mma, hd->kblk);
+                           n_out, i8 ? 64 : hd->n_mma, hd->kblk);
     if (rc != KL_OK) return rc;
+    if (i8) {
+      // the MMA's B operand is the digit planes of the tile: i8_tile_rows(T) rows of K int8
+      TcProblem& pr = tab[i];
+      const int tok = hd->n_mma;
+      pr.tok = tok;
+      pr.x_src = q.x;
+      pr.digits = static_cast<int8_t*>(digits);
+      pr.digits_ld = q.k;
+      tc_problem_tiles(pr, tok, hd->kblk, swiglu != 0);
+      const size_t planes = digits_plane_bytes(q.m, q.k, tok);
+      pr.tscale = reinterpret_cast<float*>(static_cast<char*>(digits) + planes);
+      rc = encode_2d(&pr.tmap_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, pr.digits, q.k,
+                     static_cast<uint64_t>(pr.m_tiles) * i8_tile_rows(tok), q.k, 128, i8_tile_rows(tok),
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != KL_OK) return rc;
+      digits = static_cast<char*>(digits) + planes + digits_scale_bytes(q.m, tok);
+      hd->rows_max = std::max(hd->rows_max, pr.m_tiles * tok);
+    }
     tab[i].unit_begin = units;
     units += static_cast<long long>(tab[i].m_tiles) * tab[i].n_tiles * tab[i].kb_total;
   }
@@ -483,7 +545,7 @@ size_t kl_grouped_workspace_bytes(const void* host_table) {
     sm = v;
   else
     cudaGetLastError();
-  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->w_format, sm);
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->int8_mma ? kFmtI8 : hd->w_format, sm);
   return plan.ok ? plan.workspace : 0;
 }
 
@@ -498,7 +560,7 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
   if (rc != KL_OK) return rc;
   if (!(di.major == 10 && di.minor == 0))
     return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
-  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->w_format, di.sm_count);
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->int8_mma ? kFmtI8 : hd->w_format, di.sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for the group");
   if (!workspace || workspace_bytes < plan.workspace)
     return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
@@ -519,8 +581,18 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   p.status = di.status;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (hd->int8_mma) {
+    // digits pass, then the GEMM chained to it with programmatic dependent
+    // launch (its weight stream starts while the digits are written)
+    cudaError_t e = launch_act_digits(p.table, host_tab[0], p.count, hd->rows_max, (flags & KL_FLAG_PDL) != 0, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation digits launch");
+    e = launch_tc_i8(p, plan, hd->swiglu ? kEpiSwiglu : kEpiPlain, true, st);
+    if (e != cudaSuccess) return cuda_fail(e, "grouped int8 tcgen05 GEMM launch");
+    return KL_OK;
+  }
   const cudaError_t e = launch_tc(p, plan, hd->w_format, hd->swiglu ? kEpiSwiglu : kEpiPlain, hd->x_dtype == KL_DT_BF16,
-                                  (flags & KL_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+                                  (flags & KL_FLAG_PDL) != 0, st);
   if (e != cudaSuccess) return cuda_fail(e, "grouped tcgen05 GEMM launch");
   return KL_OK;
 }

@@ -124,6 +124,17 @@ KL_DEVICE void tc_mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_desc_lo
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n}"
       :: "r"(d_tmem), "r"(a_tmem), "r"(b_desc_lo), "n"(kSmemDescSw128Hi), "r"(idesc), "r"(accumulate) : "memory");
 }
+// D[tmem] (+)= A[smem desc] * B[smem desc]; kind::i8 (signed 8-bit A and B,
+// s32 accumulate).  Both descriptors are SW128 K-major, given by their low
+// words (the high word is kSmemDescSw128Hi).
+KL_DEVICE void tc_mma_ss_i8(uint32_t d_tmem, uint32_t a_desc_lo, uint32_t b_desc_lo, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b64 ad, bd;\n setp.ne.b32 p, %4, 0;\n mov.b64 ad, {%1, %5};\n"
+      " mov.b64 bd, {%2, %5};\n tcgen05.mma.cta_group::1.kind::i8 [%0], ad, bd, %3, p;\n}"
+      :: "r"(d_tmem), "r"(a_desc_lo), "r"(b_desc_lo), "r"(idesc), "r"(accumulate), "n"(kSmemDescSw128Hi)
+      : "memory");
+}
 // ------------------------------------------------ CTA pairs (cta_group::2)
 // A 2-CTA cluster whose tensor cores run one MMA over both CTAs' operands.
 KL_DEVICE uint32_t cluster_ctarank() {
@@ -269,6 +280,13 @@ KL_DEVICE uint32_t smem_desc_sw128_lo(uint32_t saddr) { return ((saddr >> 4) & 0
 __host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, bool bf16) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor, kind::i8: s32 accumulator (bits 4-5 = 2), A and B
+// signed 8-bit (format 1 at bits 7-9 and 10-12), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t make_idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---------------------------------------------------------- int -> bf16 bits

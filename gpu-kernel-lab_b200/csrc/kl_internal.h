@@ -41,6 +41,14 @@ int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2
 constexpr int kMaxGroup = 512;        // problems per grouped launch
 constexpr int kMaxWStages = 16;
 
+// Internal format id of the int8-MMA mode of KL_W8_ROW weights (kl_tc_i8.cu):
+// the activations are split into three int8 digit planes per token and the
+// weights feed tcgen05.mma.kind::i8 without conversion.
+constexpr int kFmtI8 = 16;
+// Digit rows of one token tile of T tokens: the h, m and l planes (T rows
+// each), padded to a legal MMA N (a multiple of 16).
+__host__ __device__ constexpr int i8_tile_rows(int t) { return (3 * t + 15) / 16 * 16; }
+
 // One GEMM of a launch (256-byte aligned so it can live in a device table).
 struct alignas(64) TcProblem {
   CUtensorMap tmap_w;                 // int8 [N, K] (box 128 B x 64 rows) or u8 [N, K/2] (64 B x 64 rows)
@@ -61,6 +69,15 @@ struct alignas(64) TcProblem {
   unsigned long long* cand;
   long long index_offset;
   int topk, cand_ld;
+  // int8-MMA mode: the bf16 activations x_src [m, k] are split by the digits
+  // pass into digits [m_tiles][i8_tile_rows(T)][digits_ld] (h, m, l planes of
+  // T rows, zero padding rows) and one power-of-two scale per token,
+  // tscale [m_tiles * T]; tmap_x covers digits
+  const void* x_src;
+  int8_t* digits;
+  float* tscale;
+  long long digits_ld;
+  int tok;                            // token tile T (the MMA's N is i8_tile_rows(T))
 };
 
 struct TcParams {
@@ -92,6 +109,15 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count);
 // epilogue: 0 outputs, 1 SwiGLU outputs, 2 top-k candidates (TcProblem::cand)
 constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiTopk = 2;
 cudaError_t launch_tc(const TcParams& p, const TcPlan& plan, int fmt, int epi, bool xbf16, bool pdl, cudaStream_t s);
+// int8-MMA mode (kl_tc_i8.cu): token tile T in {8, 16, 32, 64}.
+int tc_choose_tokens_i8(int m);
+int tc_threads_i8();
+// The digits pass over every problem of a launch (host_tab: the problems, for
+// the grid; dev_tab: the same table in device memory, or null for one problem
+// passed by value), then the GEMM.
+cudaError_t launch_act_digits(const TcProblem* dev_tab, const TcProblem& single, int count, int rows_max,
+                              bool pdl, cudaStream_t s);
+cudaError_t launch_tc_i8(const TcParams& p, const TcPlan& plan, int epi, bool pdl, cudaStream_t s);
 
 // ---- dependent-chain decode GEMM: one 128-row tile per cluster (kl_tc_chain.cu)
 // For one int8 row-scale linear with M <= 64 launched after the op that

@@ -195,9 +195,22 @@ class GroupedLinear:
     launch gaps between problems.  All weights share one format (KL_W8_ROW or
     a group-128 4-bit format); SwiGLU applies to all problems or none.
     Capture ``run()`` in a CUDA graph for repeated use.
+
+    ``mma``: ``"int8"`` feeds int8 row-scale weights to the tensor core
+    unconverted (``kind::i8``) after a digits pass that writes each token row
+    as a power-of-two scale and three int8 planes (``x = s (65536 h + 256 m +
+    l)``: exact for activations within a factor 2^14 of the row's largest,
+    else within ``s / 2``); ``"bf16"`` converts the weights to bf16 in the
+    kernel.
+    ``"auto"`` (default) takes ``"int8"`` for int8 row weights with bf16
+    activations and at most 8 tokens per problem, else ``"bf16"``: the three
+    digit planes make the int8 MMA 3 tokens wide per token, which costs more
+    tensor time than the bf16 conversion saves once tiles are 16 tokens or
+    wider (measured on the config 1 set: 101 against 108 us at M = 1, 163
+    against 148 us at M = 64).
     """
 
-    def __init__(self, problems, *, swiglu: bool = False):
+    def __init__(self, problems, *, swiglu: bool = False, mma: str = "auto"):
         import ctypes
         if not problems:
             raise ValueError("at least one problem required")
@@ -223,9 +236,24 @@ class GroupedLinear:
         nbytes = lib.kl_grouped_table_bytes(len(problems))
         if nbytes == 0:
             raise ValueError("too many problems for one grouped launch")
+        if mma not in ("auto", "int8", "bf16"):
+            raise ValueError(f"mma must be 'auto', 'int8' or 'bf16', not {mma!r}")
+        if mma == "auto":
+            max_m = max(x.numel() // spec[6] for (x, _, _), spec in zip(problems, specs))
+            mma = "int8" if (fmt == N.KL_W8_ROW and x0.dtype == torch.bfloat16 and max_m <= 8) else "bf16"
+        self.mma = mma
+        flags = N.KL_GROUPED_INT8_MMA if mma == "int8" else 0
+        self._digits = None
+        dptr, dbytes = None, 0
+        if flags:
+            dbytes = lib.kl_grouped_digits_bytes(arr, len(problems), flags)
+            if dbytes == 0:
+                raise ValueError("no digits layout for these problems")
+            self._digits = torch.empty(dbytes + 256, dtype=torch.uint8, device=self.device)
+            dptr = self._digits.data_ptr() + (-self._digits.data_ptr()) % 256
         self._host = (ctypes.c_uint8 * nbytes)()
-        N.check(lib.kl_grouped_encode(arr, len(problems), N.act_dtype_code(x0.dtype), fmt, int(swiglu),
-                                      self._host, nbytes))
+        N.check(lib.kl_grouped_encode_ex(arr, len(problems), N.act_dtype_code(x0.dtype), fmt, int(swiglu), flags,
+                                         dptr, dbytes, self._host, nbytes))
         host_t = torch.frombuffer(self._host, dtype=torch.uint8)
         self._device = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.device)
         off = (-self._device.data_ptr()) % 256

@@ -141,6 +141,27 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
                       size_t workspace_bytes, int flags, void* stream);
 
 /*
+ * Int8 tensor-core mode of the grouped launch (KL_W8_ROW weights, bf16
+ * activations).  No reference counterpart: the same computation as the
+ * default mode, with the weights fed to tcgen05.mma.kind::i8 unconverted.
+ * kl_linear_grouped then runs two kernels on the stream: a digits pass that
+ * writes every token row as a power-of-two scale s_t = 2^(floor(log2 max|x|) - 21)
+ * and three int8 planes h, m, l with x = s_t * (65536 h + 256 m + l) (exact
+ * for every activation within a factor 2^14 of its token's largest, else
+ * within s_t / 2), then the GEMM.  `digits` is a caller-owned, 256-byte-aligned
+ * DEVICE buffer of kl_grouped_digits_bytes(...) bytes that stays fixed for
+ * the life of the table (its address is in the table's tensor maps); calls
+ * that share it must not overlap.  A token whose largest |x| is not finite
+ * gets NaN outputs.
+ *   flags: KL_GROUPED_INT8_MMA, or 0 for kl_grouped_encode's default mode
+ *   (digits ignored).
+ */
+#define KL_GROUPED_INT8_MMA 1
+size_t kl_grouped_digits_bytes(const kl_problem* problems, int count, int flags);
+int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int w_format, int swiglu, int flags,
+                         void* digits, size_t digits_bytes, void* host_table, size_t table_bytes);
+
+/*
  * The reference's op, same arguments and checks (warp_gemv.cu:56-72):
  *   x bf16 [K]; w int8 [N,K] (w_is_int8 = 1, with f32 scales [N,K/group] and
  *   f32 inverse [K]) or bf16 [N,K] (w_is_int8 = 0, scales/inverse ignored);
