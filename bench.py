@@ -754,8 +754,22 @@ def section_prefill(kl, weights, device, tf_burst, peak_kind, args, rank, world,
                 tfs = flops / (ms * 1e-3) / 1e12
                 row["swiglu" if sw else "plain"] = {"ms": round(ms, 3), "TFLOP/s": round(tfs, 1),
                                                     "frac": round(tfs / tf_burst, 3)}
+            del xs, ys, items
+            # the same 112 GEMMs with independent activations and outputs as ONE
+            # grouped launch on the CTA-pair kernel (the config 1 treatment)
+            probs = [(torch.randn(m, p.shape[1], device=device, generator=gen).to(torch.bfloat16), p,
+                      torch.empty(m, p.shape[0], device=device, dtype=torch.bfloat16)) for _, p in weights]
+            grp = kl.GroupedLinear(probs)
+            grp.run(pdl=True)
+            torch.cuda.synchronize()
+            g = capture(lambda: grp.run(pdl=True))
+            ms = max_over_ranks(timed(g, 3 if m == 8192 else 5), dist, device)
+            del g, grp
+            flops = sum(2 * m * p.shape[0] * p.shape[1] for _, p in weights)
+            tfs = flops / (ms * 1e-3) / 1e12
+            row["grouped"] = {"ms": round(ms, 3), "TFLOP/s": round(tfs, 1), "frac": round(tfs / tf_burst, 3)}
+            del probs
             res[str(m)] = row
-            del xs
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # the reference's CPU path (dequantise + fp32 matmul + bf16 cast) on a subset:
@@ -780,7 +794,8 @@ def section_prefill(kl, weights, device, tf_burst, peak_kind, args, rank, world,
         cpu = {"value": round(flops / t_total / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"M=512 against 1024-row slices of the qkv/o/gate_up/down shapes ({t_total:.1f} s)"}
     return {"unit": "TFLOP/s", "peak": tf_burst, "peak_source": peak_kind, "batch_m": ms_list,
-            "launch": "28 layers x 4 GEMMs per M in model order, programmatic dependent launch, one CUDA graph",
+            "launch": ("plain / swiglu: 28 layers x 4 GEMMs per M in model order, programmatic dependent launch, "
+                       "one CUDA graph; grouped: the 112 GEMMs with independent activations as one CTA-pair launch"),
             "per_m": res, "cpu_baseline": cpu, "clocks": clocks.summary()}
 
 

@@ -411,8 +411,10 @@ struct GroupHeader {
   int kblk;
   int int8_mma;                     // 1: KL_GROUPED_INT8_MMA (digits pass + kind::i8 GEMM)
   int rows_max;                     // int8 mode: largest m_tiles * T of the problems
-  uint8_t pad[256 - 44];
+  int pair;                         // 1: every problem runs on the CTA-pair prefill kernel (table of PfParams)
+  uint8_t pad[256 - 48];
 };
+static_assert(sizeof(PfParams) <= sizeof(TcProblem), "a pair-mode table fits the table size");
 static_assert(sizeof(GroupHeader) == 256, "group header");
 constexpr uint32_t kGroupMagic = 0x4B4C4752u;   // "KLGR"
 }  // namespace
@@ -486,6 +488,51 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
   std::memset(hd, 0, sizeof(*hd));
   hd->magic = kGroupMagic;
   hd->count = static_cast<uint32_t>(count);
+  int sm_pair = 148, dev_pair = 0, v_pair = 0;
+  if (cudaGetDevice(&dev_pair) == cudaSuccess &&
+      cudaDeviceGetAttribute(&v_pair, cudaDevAttrMultiProcessorCount, dev_pair) == cudaSuccess && v_pair > 0)
+    sm_pair = v_pair;
+  else
+    cudaGetLastError();
+  // many-token groups: every problem on the CTA-pair kernel, the tiles of all
+  // problems dealt round-robin to the pairs of one launch
+  bool pair = !i8;
+  for (int i = 0; i < count && pair; ++i)
+    pair = prefill_applies(problems[i].m, problems[i].k, w_format, sm_pair);
+  if (pair) {
+    hd->pair = 1;
+    hd->w_format = w_format;
+    hd->swiglu = swiglu ? 1 : 0;
+    hd->x_dtype = x_dtype;
+    PfParams* tab = reinterpret_cast<PfParams*>(hd + 1);
+    for (int i = 0; i < count; ++i) {
+      const kl_problem& q = problems[i];
+      PfParams& p = tab[i];
+      std::memset(&p, 0, sizeof(p));
+      p.scales = q.scales;
+      p.y = q.y;
+      p.m = q.m;
+      p.n = q.n;
+      p.k = q.k;
+      p.n_out = swiglu ? q.n / 2 : q.n;
+      p.ldy = p.n_out;
+      p.vec_store = (aligned16(q.y) && p.ldy % 8 == 0) ? 1 : 0;
+    }
+    const int tiles = prefill_group_tiles(tab, count, swiglu != 0, sm_pair);
+    for (int i = 0; i < count; ++i) {
+      const kl_problem& q = problems[i];
+      PfParams& p = tab[i];
+      int rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.w, q.k, q.n, q.k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc != KL_OK) return rc;
+      rc = encode_2d(&p.tmap_x, x_dtype == KL_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     q.x, q.k, q.m, static_cast<uint64_t>(q.k) * act_bytes(x_dtype), 64,
+                     static_cast<uint32_t>(p.tok / 2), CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != KL_OK) return rc;
+    }
+    hd->n_mma = tab[0].tok;
+    hd->units = tiles;
+    return KL_OK;
+  }
   hd->n_mma = i8 ? tc_choose_tokens_i8(max_m) : tc_choose_nmma(max_m, w_format);
   hd->int8_mma = i8 ? 1 : 0;
   hd->w_format = w_format;
@@ -540,6 +587,7 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
 size_t kl_grouped_workspace_bytes(const void* host_table) {
   const GroupHeader* hd = static_cast<const GroupHeader*>(host_table);
   if (!hd || hd->magic != kGroupMagic) return 0;
+  if (hd->pair) return 0;                       // whole-K tiles: no split-tile scratch
   int sm = 148, dev = 0, v = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
     sm = v;
@@ -560,6 +608,23 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
   if (rc != KL_OK) return rc;
   if (!(di.major == 10 && di.minor == 0))
     return fail(KL_ERR_UNSUPPORTED, "this library is built for sm_100a (device is sm%d%d)", di.major, di.minor);
+  if (hd->pair) {
+    const PfParams* host_pf = reinterpret_cast<const PfParams*>(hd + 1);
+    PfLaunch l;
+    std::memset(&l, 0, sizeof(l));
+    l.single = host_pf[0];
+    l.single.status = di.status;
+    l.count = static_cast<int>(hd->count);
+    l.table = l.count > 1 ? reinterpret_cast<const PfParams*>(static_cast<const char*>(device_table) + sizeof(GroupHeader))
+                          : nullptr;
+    l.tiles = static_cast<int>(hd->units);
+    l.status = di.status;
+    const int grid = 2 * std::max(1, std::min(l.tiles, di.sm_count / 2));
+    const cudaError_t e = launch_prefill_group(l, grid, hd->swiglu != 0, hd->x_dtype == KL_DT_BF16,
+                                               (flags & KL_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "grouped tcgen05 pair GEMM launch");
+    return KL_OK;
+  }
   const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->int8_mma ? kFmtI8 : hd->w_format, di.sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for the group");
   if (!workspace || workspace_bytes < plan.workspace)

@@ -189,6 +189,17 @@ struct PfParams {
   int y_transposed;
   int vec_store;                      // y 16-byte aligned, ldy % 8 == 0: 16-byte stores (1 row-major, 2 transposed)
   int* status;
+  int tile_begin;                     // grouped launches: first global tile of this problem
+};
+// One launch of the pair kernel: one problem, or a device table of problems
+// (same SwiGLU mode, activation type and token tile) whose tiles are dealt out
+// round-robin to the CTA pairs as one sequence.
+struct PfLaunch {
+  PfParams single;                    // the problem when count == 1
+  const PfParams* table;              // device table when count > 1 (64-byte-aligned entries)
+  int count;
+  int tiles;                          // tiles of all problems
+  int* status;
 };
 int prefill_threads();
 int prefill_smem_bytes(int tok);
@@ -197,6 +208,10 @@ int prefill_choose_tokens(int m, int n_tiles, int sm_count);
 void prefill_tiles(PfParams& p, bool swiglu, int sm_count);
 int prefill_grid(const PfParams& p, int sm_count);
 cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
+// Token tile for a group of problems (fills each problem's n_tiles / m_tiles /
+// kb_total / tok / tile_begin; returns the total tiles).
+int prefill_group_tiles(PfParams* probs, int count, bool swiglu, int sm_count);
+cudaError_t launch_prefill_group(const PfLaunch& l, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s);
 
 // Work partition shared by the kernel and the host-side self-check:
 // CTA c owns units [lo(c), lo(c+1)) with lo(c) = floor(c * units / grid).

@@ -24,6 +24,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "kl_common.cuh"
 #include "kl_internal.h"
@@ -52,7 +53,7 @@ constexpr int kPfStageBytes = 32 * kPfChunk * 2; // per epilogue warp: 32 rows x
 static_assert(kPfDCol0 + 2 * kPfMaxTokens == 512, "TMEM budget");
 
 struct PfLayout {
-  uint32_t w, x, xch, stage, bars, misc, total;
+  uint32_t w, x, xch, stage, tcache, bars, misc, total;
 };
 constexpr PfLayout pf_layout(int tok) {
   PfLayout l{};
@@ -60,7 +61,8 @@ constexpr PfLayout pf_layout(int tok) {
   l.x = l.w + kPfW * kPfWStage;
   l.xch = l.x + kPfX * pf_xstage(tok);
   l.stage = l.xch + kPfXchFloats * 4;
-  l.bars = l.stage + 4 * kPfStageBytes;
+  l.tcache = l.stage + 4 * kPfStageBytes;        // grouped launches: each problem's first tile
+  l.bars = l.tcache + 4 * kMaxGroup;
   // w_full, w_empty [W]; x_full, x_empty [X]; a_full, a_empty [A]; d_full, d_empty [2]; done
   l.misc = l.bars + 8 * (2 * kPfW + 2 * kPfX + 2 * kPfA + 5);
   l.total = l.misc + 16 + 1024;
@@ -138,8 +140,20 @@ KL_DEVICE void pf_emit(const PfParams& p, uint8_t* stage, int col0, int ncols, i
   }
 }
 
+// Walks one role's tiles (increasing global tile index) through the problems
+// of a launch: the problem of tile t is the last one whose first tile is <= t.
+struct PfCursor {
+  const PfLaunch* l;
+  const int* tbegin;                   // shared-memory copy of the problems' tile_begin
+  int prob;
+  KL_DEVICE const PfParams& get() const { return l->count == 1 ? l->single : l->table[prob]; }
+  KL_DEVICE void seek(int t) {
+    while (prob + 1 < l->count && tbegin[prob + 1] <= t) ++prob;
+  }
+};
+
 template <bool SWIGLU, bool XBF16, int TOK>
-__global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_constant__ PfParams p) {
+__global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_constant__ PfLaunch pl) {
   constexpr int kPfTokens = TOK;                 // tokens per tile (MMA N)
   constexpr int kPfHalf = TOK / 2;               // tokens per CTA
   constexpr int kPfXStage = pf_xstage(TOK);
@@ -151,10 +165,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
-  const int tiles = p.n_tiles * p.m_tiles;
-  const int kbs = p.kb_total;
+  const int tiles = pl.tiles;
+  int* const status = pl.status;
   int my_tiles = 0;
   if (pair < tiles) my_tiles = (tiles - 1 - pair) / pairs + 1;
+  int* tbegin = reinterpret_cast<int*>(smem + L.tcache);
+  if (pl.count > 1)
+    for (int i = threadIdx.x; i < pl.count; i += blockDim.x) tbegin[i] = pl.table[i].tile_begin;
+  // (visible to every role after the cluster barrier below)
 
   const uint32_t s_w = smem_u32(smem + L.w), s_x = smem_u32(smem + L.x);
   const uint32_t bars = smem_u32(smem + L.bars);
@@ -191,15 +209,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   if (warp == 0) {
     // ---------------------------------------------------------- weight TMA
     if (lane == 0 && my_tiles > 0) {
-      prefetch_tmap(&p.tmap_w);
       PfPipe pw{0, kPfW, 0};
+      PfCursor cur{&pl, tbegin, 0};
+      int last_prob = -1;
       for (int it = 0; it < my_tiles; ++it) {
         const int t = pair + it * pairs;
-        const int nt = t % p.n_tiles;
+        cur.seek(t);
+        const PfParams& p = cur.get();
+        if (cur.prob != last_prob) { prefetch_tmap(&p.tmap_w); last_prob = cur.prob; }
+        const int nt = (t - p.tile_begin) % p.n_tiles;
+        const int kbs = p.kb_total;
         const int y0 = SWIGLU ? nt * 128 + static_cast<int>(rank) * 64 : nt * 256 + static_cast<int>(rank) * 128;
         const int y1 = SWIGLU ? p.n_out + y0 : y0 + 64;
         for (int kb = 0; kb < kbs; ++kb) {
-          if (!pf_wait(w_empty(pw.idx), pw.phase ^ 1u, p.status)) { it = my_tiles; break; }
+          if (!pf_wait(w_empty(pw.idx), pw.phase ^ 1u, status)) { it = my_tiles; break; }
           const uint32_t dst = s_w + pw.idx * kPfWStage;
           mbar_arrive_expect_tx(w_full(pw.idx), kPfWStage);
           tma_load_2d(dst, &p.tmap_w, kb * kPfKb, y0, w_full(pw.idx));
@@ -211,16 +234,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   } else if (warp == 1) {
     // ----------------------------------------------------------- token TMA
     if (lane == 0 && my_tiles > 0) {
-      prefetch_tmap(&p.tmap_x);
       pdl_wait();                              // tokens come from the previous kernel
       const uint32_t lead_full0 = mapa_shared(x_full(0), 0);
       PfPipe px{0, kPfX, 0};
+      PfCursor cur{&pl, tbegin, 0};
+      int last_prob = -1;
       for (int it = 0; it < my_tiles; ++it) {
         const int t = pair + it * pairs;
-        const int mt = t / p.n_tiles;
+        cur.seek(t);
+        const PfParams& p = cur.get();
+        if (cur.prob != last_prob) { prefetch_tmap(&p.tmap_x); last_prob = cur.prob; }
+        const int mt = (t - p.tile_begin) / p.n_tiles;
+        const int kbs = p.kb_total;
         const int row = mt * kPfTokens + static_cast<int>(rank) * kPfHalf;
         for (int kb = 0; kb < kbs; ++kb) {
-          if (!pf_wait(x_empty(px.idx), px.phase ^ 1u, p.status)) { it = my_tiles; break; }
+          if (!pf_wait(x_empty(px.idx), px.phase ^ 1u, status)) { it = my_tiles; break; }
           if (leader) mbar_arrive_expect_tx(x_full(px.idx), 2 * kPfXStage);
           tma_load_2d_pair(s_x + px.idx * kPfXStage, &p.tmap_x, kb * kPfKb, row, lead_full0 + 8u * px.idx);
           px.next();
@@ -233,14 +261,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
       constexpr uint32_t idesc = make_idesc_f16(256, kPfTokens, XBF16);
       const uint32_t x_desc0 = smem_desc_sw128_lo(s_x);
       PfPipe px{0, kPfX, 0}, pa{0, kPfA, 0}, pd{0, 2, 0};
+      PfCursor cur{&pl, tbegin, 0};
       bool ok = true;
       for (int it = 0; it < my_tiles && ok; ++it) {
-        if (!(ok = pf_wait_warp(d_empty(pd.idx), pd.phase ^ 1u, p.status))) break;
+        cur.seek(pair + it * pairs);
+        const int kbs = cur.get().kb_total;
+        if (!(ok = pf_wait_warp(d_empty(pd.idx), pd.phase ^ 1u, status))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + kPfDCol0 + pd.idx * kPfTokens;
         for (int kb = 0; kb < kbs; ++kb) {
-          if (!(ok = pf_wait_warp(x_full(px.idx), px.phase, p.status))) break;
-          if (!(ok = pf_wait_warp(a_full(pa.idx), pa.phase, p.status))) break;
+          if (!(ok = pf_wait_warp(x_full(px.idx), px.phase, status))) break;
+          if (!(ok = pf_wait_warp(a_full(pa.idx), pa.phase, status))) break;
           tc_fence_after();
           const uint32_t a_tmem = tmem + pa.idx * kPfACols;
           const uint32_t xd = x_desc0 + static_cast<uint32_t>(px.idx * (kPfXStage >> 4));
@@ -268,11 +299,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
     const int r = q * 32 + lane;               // weight row of this CTA's 128
     const uint32_t lead_a_full0 = mapa_shared(a_full(0), 0);
     PfPipe pw{0, kPfW, 0}, pa{0, kPfA, 0};
+    PfCursor cur{&pl, tbegin, 0};
     for (int it = 0; it < my_tiles; ++it) {
       bool ok = true;
+      cur.seek(pair + it * pairs);
+      const int kbs = cur.get().kb_total;
       for (int kb = 0; kb < kbs; ++kb) {
-        if (!(ok = pf_wait(w_full(pw.idx), pw.phase, p.status))) break;
-        if (!(ok = pf_wait(a_empty(pa.idx), pa.phase ^ 1u, p.status))) break;
+        if (!(ok = pf_wait(w_full(pw.idx), pw.phase, status))) break;
+        if (!(ok = pf_wait(a_empty(pa.idx), pa.phase ^ 1u, status))) break;
         tc_fence_after();
         const uint8_t* ws = smem + L.w + pw.idx * kPfWStage;
         uint32_t part[16];
@@ -308,11 +342,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
     uint8_t* stg = smem + L.stage + (warp - kPfEpi0) * kPfStageBytes;
     pdl_wait();                                // y is written only after the previous kernel
     PfPipe pd{0, 2, 0};
+    PfCursor cur{&pl, tbegin, 0};
     for (int it = 0; it < my_tiles; ++it) {
       const int t = pair + it * pairs;
-      const int nt = t % p.n_tiles, mt = t / p.n_tiles;
+      cur.seek(t);
+      const PfParams& p = cur.get();
+      const int lt = t - p.tile_begin;
+      const int nt = lt % p.n_tiles, mt = lt / p.n_tiles;
       // the 4 epilogue warps take the same decision (they share named barriers)
-      const bool got = pf_wait(d_full(pd.idx), pd.phase, p.status);
+      const bool got = pf_wait(d_full(pd.idx), pd.phase, status);
       uint32_t all_got;
       asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 2, 128, q;\n selp.u32 %0, 1, 0, p;\n}"
                    : "=r"(all_got) : "r"(got ? 1u : 0u) : "memory");
@@ -374,7 +412,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
 
   // ---- teardown: every MMA of the pair has completed before TMEM is freed
   if (warp == 2) {
-    if (my_tiles > 0 && !mbar_wait_time(done_bar, 0)) record_error(p.status, KL_ERR_TIMEOUT);
+    if (my_tiles > 0 && !mbar_wait_time(done_bar, 0)) record_error(status, KL_ERR_TIMEOUT);
   }
   __syncwarp();
   tc_fence_before();
@@ -383,7 +421,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
 }
 
 template <bool SWIGLU, bool XBF16, int TOK>
-cudaError_t launch_pf(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
+cudaError_t launch_pf(const PfLaunch& p, int grid, bool pdl, cudaStream_t s) {
   auto kern = tc_prefill_kernel<SWIGLU, XBF16, TOK>;
   constexpr int smem = static_cast<int>(pf_layout(TOK).total);
   static bool attr[kMaxDevices] = {};
@@ -470,18 +508,63 @@ int prefill_grid(const PfParams& p, int sm_count) {
 }
 
 template <bool SWIGLU, bool XBF16>
-cudaError_t launch_tok(const PfParams& p, int grid, bool pdl, cudaStream_t s) {
-  switch (p.tok) {
-    case 192: return launch_pf<SWIGLU, XBF16, 192>(p, grid, pdl, s);
-    case 128: return launch_pf<SWIGLU, XBF16, 128>(p, grid, pdl, s);
-    case 64: return launch_pf<SWIGLU, XBF16, 64>(p, grid, pdl, s);
+cudaError_t launch_tok(const PfLaunch& l, int tok, int grid, bool pdl, cudaStream_t s) {
+  switch (tok) {
+    case 192: return launch_pf<SWIGLU, XBF16, 192>(l, grid, pdl, s);
+    case 128: return launch_pf<SWIGLU, XBF16, 128>(l, grid, pdl, s);
+    case 64: return launch_pf<SWIGLU, XBF16, 64>(l, grid, pdl, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
+cudaError_t launch_prefill_group(const PfLaunch& l, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s) {
+  const int tok = l.single.tok;
+  if (swiglu) return xbf16 ? launch_tok<true, true>(l, tok, grid, pdl, s) : launch_tok<true, false>(l, tok, grid, pdl, s);
+  return xbf16 ? launch_tok<false, true>(l, tok, grid, pdl, s) : launch_tok<false, false>(l, tok, grid, pdl, s);
+}
+
 cudaError_t launch_prefill(const PfParams& p, int grid, bool swiglu, bool xbf16, bool pdl, cudaStream_t s) {
-  if (swiglu) return xbf16 ? launch_tok<true, true>(p, grid, pdl, s) : launch_tok<true, false>(p, grid, pdl, s);
-  return xbf16 ? launch_tok<false, true>(p, grid, pdl, s) : launch_tok<false, false>(p, grid, pdl, s);
+  PfLaunch l;
+  std::memset(&l, 0, sizeof(l));
+  l.single = p;
+  l.single.tile_begin = 0;
+  l.table = nullptr;
+  l.count = 1;
+  l.tiles = p.n_tiles * p.m_tiles;
+  l.status = p.status;
+  return launch_prefill_group(l, grid, swiglu, xbf16, pdl, s);
+}
+
+// Token tile for a group: every problem gets the same tile; the choice
+// minimises (tile-K-blocks per pair, rounded up) x the per-K-block cost of a
+// tile, max(tok + 48, 192) token-steps (see prefill_choose_tokens).
+int prefill_group_tiles(PfParams* probs, int count, bool swiglu, int sm_count) {
+  const int pairs = std::max(1, sm_count / 2);
+  int best = kPfMaxTokens;
+  long long best_cost = -1;
+  for (int tok : {192, 128, 64}) {
+    long long work = 0;                  // tile x K-block units
+    for (int i = 0; i < count; ++i) {
+      const int n_tiles = swiglu ? (probs[i].n_out + 127) / 128 : (probs[i].n + 255) / 256;
+      work += static_cast<long long>(n_tiles) * ((probs[i].m + tok - 1) / tok) * (probs[i].k / kPfKb);
+    }
+    const long long cost = ((work + pairs - 1) / pairs) * std::max(tok + 48, 192);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = tok;
+    }
+  }
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    PfParams& p = probs[i];
+    p.n_tiles = swiglu ? (p.n_out + 127) / 128 : (p.n + 255) / 256;
+    p.tok = best;
+    p.m_tiles = (p.m + best - 1) / best;
+    p.kb_total = p.k / kPfKb;
+    p.tile_begin = tiles;
+    tiles += p.n_tiles * p.m_tiles;
+  }
+  return tiles;
 }
 
 }  // namespace kl

@@ -202,6 +202,9 @@ class GroupedLinear:
     l)``: exact for activations within a factor 2^14 of the row's largest,
     else within ``s / 2``); ``"bf16"`` converts the weights to bf16 in the
     kernel.
+    Groups whose every problem has at least 256 tokens (int8 row weights,
+    K a multiple of 64) run on the CTA-pair prefill kernel instead, the tiles
+    of all problems in one launch (unless ``mma="int8"``).
     ``"auto"`` (default) takes ``"int8"`` for int8 row weights with bf16
     activations and at most 8 tokens per problem, else ``"bf16"``: the three
     digit planes make the int8 MMA 3 tokens wide per token, which costs more
@@ -267,7 +270,7 @@ class GroupedLinear:
     def run(self, *, pdl: bool = False, workspace: torch.Tensor | None = None):
         lib = N.lib()
         ws = workspace if workspace is not None else N.workspace(self.device, self._ws_bytes)
+        ws_bytes = 0 if ws is None else ws.numel() * ws.element_size()
         with torch.cuda.device(self.device):
-            N.check(lib.kl_linear_grouped(self._host, N.ptr(self._dev_view), N.ptr(ws),
-                                          ws.numel() * ws.element_size(), N.KL_FLAG_PDL if pdl else 0,
-                                          N.stream_handle(self.device)))
+            N.check(lib.kl_linear_grouped(self._host, N.ptr(self._dev_view), N.ptr(ws), ws_bytes,
+                                          N.KL_FLAG_PDL if pdl else 0, N.stream_handle(self.device)))

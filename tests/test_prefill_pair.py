@@ -102,3 +102,78 @@ def test_pdl_chain_reads_previous_output():
     torch.cuda.synchronize()
     assert_matches_oracle(y1, ref(x, q1, s1), what="pdl first")
     assert_matches_oracle(y2, ref(y1.cpu(), q2, s2), what="pdl second")
+
+
+# ---- grouped launches on the pair kernel (every problem M >= 256, K % 64 == 0)
+
+def _grouped(problems, swiglu=False):
+    g = kl.GroupedLinear(problems, swiglu=swiglu)
+    g.run()
+    torch.cuda.synchronize()
+    assert N.device_status(torch.cuda.current_device()) == 0
+    return g
+
+
+@pytest.mark.parametrize("m", [256, 300, 512])
+def test_grouped_pair_layer(m):
+    """A Qwen3 layer's four GEMMs plus ragged shapes in one pair launch."""
+    shapes = [(4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (520, 640), (130, 192)]
+    probs, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        x, p, q, s = make(m, n, k, seed=1000 + i + m)
+        probs.append((x.cuda(), p, torch.empty(m, n, device="cuda", dtype=torch.bfloat16)))
+        refs.append(ref(x, q, s))
+    _grouped(probs)
+    for (_, p, y), r in zip(probs, refs):
+        assert_matches_oracle(y, r, what=f"grouped pair {tuple(p.data.shape)} m={m}")
+
+
+def test_grouped_pair_swiglu_and_f16():
+    m = 320
+    probs, refs = [], []
+    for i in range(2):
+        x, p, q, s = make(m, 6144, 1024, seed=1100 + i)
+        probs.append((x.cuda(), p, torch.empty(m, 3072, device="cuda", dtype=torch.bfloat16)))
+        refs.append(O.swiglu(O.bf16_round(ref(x, q, s))))
+    _grouped(probs, swiglu=True)
+    for (_, _, y), r in zip(probs, refs):
+        assert_matches_oracle(y, r, what="grouped pair swiglu")
+    x, p, q, s = make(256, 1024, 1024, seed=1200, dtype=torch.float16)
+    y = torch.empty(256, 1024, device="cuda", dtype=torch.float16)
+    _grouped([(x.cuda(), p, y), (x.cuda(), p, torch.empty_like(y))])
+    assert_matches_oracle(y, ref(x, q, s), what="grouped pair f16")
+
+
+def test_grouped_pair_matches_single_calls_and_replays():
+    """Whole-K tiles: the grouped launch gives the same bits as one call per
+    problem, eagerly and when replayed from a CUDA graph."""
+    m = 512
+    probs = []
+    for i, (n, k) in enumerate([(4096, 1024), (1024, 2048), (1024, 3072)]):
+        x, p, _, _ = make(m, n, k, seed=1300 + i)
+        probs.append((x.cuda(), p, torch.empty(m, n, device="cuda", dtype=torch.bfloat16)))
+    g = _grouped(probs)
+    for x, p, y in probs:
+        assert torch.equal(kl.quant_linear(x, p), y)
+    graph = torch.cuda.CUDAGraph()
+    first = [y.clone() for _, _, y in probs]
+    with torch.cuda.graph(graph):
+        g.run(pdl=True)
+    for _, _, y in probs:
+        y.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, (_, _, y) in zip(first, probs):
+        assert torch.equal(a, y)
+
+
+def test_grouped_mixed_m_stays_on_stream_k():
+    """A group with any problem under 256 tokens keeps the stream-K kernel."""
+    probs, refs = [], []
+    for i, m in enumerate([256, 64]):
+        x, p, q, s = make(m, 1024, 1024, seed=1400 + i)
+        probs.append((x.cuda(), p, torch.empty(m, 1024, device="cuda", dtype=torch.bfloat16)))
+        refs.append(ref(x, q, s))
+    _grouped(probs)
+    for (_, _, y), r in zip(probs, refs):
+        assert_matches_oracle(y, r, what="mixed-m group")
