@@ -460,8 +460,16 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
   if (flags & ~KL_GROUPED_INT8_MMA) return fail(KL_ERR_INVALID, "unknown grouped flags 0x%x", flags);
   const bool i8 = (flags & KL_GROUPED_INT8_MMA) != 0;
   if (i8) {
-    if (w_format != KL_W8_ROW || x_dtype != KL_DT_BF16)
-      return fail(KL_ERR_UNSUPPORTED, "the int8-MMA mode takes KL_W8_ROW weights and bf16 activations");
+    if (!(w_format == KL_W8_ROW || w_format == KL_W4_ASYM) || x_dtype != KL_DT_BF16)
+      return fail(KL_ERR_UNSUPPORTED, "the int8-MMA mode takes KL_W8_ROW or KL_W4_ASYM weights and bf16 activations");
+    if (w_format == KL_W4_ASYM) {
+      int mm = 0;
+      for (int i = 0; i < count; ++i) {
+        mm = std::max(mm, problems[i].m);
+        if (problems[i].group != 128) return fail(KL_ERR_UNSUPPORTED, "the int8-MMA 4-bit mode takes group 128");
+      }
+      if (mm > 16) return fail(KL_ERR_UNSUPPORTED, "the int8-MMA 4-bit mode takes m <= 16");
+    }
     if (!digits || (reinterpret_cast<uintptr_t>(digits) & 255u))
       return fail(KL_ERR_INVALID, "the int8-MMA mode needs a 256-byte-aligned digits buffer");
     const size_t need = kl_grouped_digits_bytes(problems, count, flags);
@@ -534,7 +542,7 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
     return KL_OK;
   }
   hd->n_mma = i8 ? tc_choose_tokens_i8(max_m) : tc_choose_nmma(max_m, w_format);
-  hd->int8_mma = i8 ? 1 : 0;
+  hd->int8_mma = i8 ? (w_format == KL_W4_ASYM ? 2 : 1) : 0;
   hd->w_format = w_format;
   hd->swiglu = swiglu ? 1 : 0;
   hd->x_dtype = x_dtype;
@@ -547,7 +555,7 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
   long long units256 = 0;
   for (int i = 0; i < count; ++i)
     units256 += problem_units(problems[i].m, problems[i].n, problems[i].k, hd->n_mma, 256, swiglu != 0);
-  hd->kblk = tc_choose_kblk(i8 ? kFmtI8 : w_format, hd->n_mma, units256, sm);
+  hd->kblk = hd->int8_mma == 2 ? 128 : tc_choose_kblk(i8 ? kFmtI8 : w_format, hd->n_mma, units256, sm);
   if (hd->kblk == 256 && is_w4(w_format)) {   // two 128-groups per stage: every problem must qualify
     for (int i = 0; i < count; ++i)
       if (!two_group_ok(w_format, problems[i].k, problems[i].zeros)) hd->kblk = 128;
@@ -593,7 +601,8 @@ size_t kl_grouped_workspace_bytes(const void* host_table) {
     sm = v;
   else
     cudaGetLastError();
-  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->int8_mma ? kFmtI8 : hd->w_format, sm);
+  const int fmt = hd->int8_mma == 2 ? kFmtI8W4 : hd->int8_mma ? kFmtI8 : hd->w_format;
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, fmt, sm);
   return plan.ok ? plan.workspace : 0;
 }
 
@@ -625,7 +634,8 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
     if (e != cudaSuccess) return cuda_fail(e, "grouped tcgen05 pair GEMM launch");
     return KL_OK;
   }
-  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, hd->int8_mma ? kFmtI8 : hd->w_format, di.sm_count);
+  const int fmt = hd->int8_mma == 2 ? kFmtI8W4 : hd->int8_mma ? kFmtI8 : hd->w_format;
+  const TcPlan plan = plan_tc(hd->n_mma, hd->kblk, hd->units, fmt, di.sm_count);
   if (!plan.ok) return fail(KL_ERR_UNSUPPORTED, "no tcgen05 plan for the group");
   if (!workspace || workspace_bytes < plan.workspace)
     return fail(KL_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", plan.workspace,
@@ -652,7 +662,7 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
     // launch (its weight stream starts while the digits are written)
     cudaError_t e = launch_act_digits(p.table, host_tab[0], p.count, hd->rows_max, (flags & KL_FLAG_PDL) != 0, st);
     if (e != cudaSuccess) return cuda_fail(e, "activation digits launch");
-    e = launch_tc_i8(p, plan, hd->swiglu ? kEpiSwiglu : kEpiPlain, true, st);
+    e = launch_tc_i8(p, plan, fmt, hd->swiglu ? kEpiSwiglu : kEpiPlain, true, st);
     if (e != cudaSuccess) return cuda_fail(e, "grouped int8 tcgen05 GEMM launch");
     return KL_OK;
   }

@@ -135,6 +135,15 @@ KL_DEVICE void tc_mma_ss_i8(uint32_t d_tmem, uint32_t a_desc_lo, uint32_t b_desc
       :: "r"(d_tmem), "r"(a_desc_lo), "r"(b_desc_lo), "r"(idesc), "r"(accumulate), "n"(kSmemDescSw128Hi)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc]; kind::i8 (A: four signed 8-bit values
+// per TMEM column along K; B: SW128 K-major, low descriptor word given).
+KL_DEVICE void tc_mma_ts_i8_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_desc_lo, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b64 bd;\n setp.ne.b32 p, %5, 0;\n mov.b64 bd, {%2, %3};\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], bd, %4, p;\n}"
+      :: "r"(d_tmem), "r"(a_tmem), "r"(b_desc_lo), "n"(kSmemDescSw128Hi), "r"(idesc), "r"(accumulate) : "memory");
+}
 // ------------------------------------------------ CTA pairs (cta_group::2)
 // A 2-CTA cluster whose tensor cores run one MMA over both CTAs' operands.
 KL_DEVICE uint32_t cluster_ctarank() {

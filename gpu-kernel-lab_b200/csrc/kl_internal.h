@@ -45,6 +45,10 @@ constexpr int kMaxWStages = 16;
 // the activations are split into three int8 digit planes per token and the
 // weights feed tcgen05.mma.kind::i8 without conversion.
 constexpr int kFmtI8 = 16;
+// Internal format id of the int8-MMA mode of asymmetric 4-bit weights
+// (KL_W4_ASYM, group 128): nibbles become int8 (q - z) in TMEM, one 128-group
+// per stage and accumulator, the same digit planes as kFmtI8.
+constexpr int kFmtI8W4 = 17;
 // Digit rows of one token tile of T tokens: the h, m and l planes (T rows
 // each), padded to a legal MMA N (a multiple of 16).
 __host__ __device__ constexpr int i8_tile_rows(int t) { return (3 * t + 15) / 16 * 16; }
@@ -117,7 +121,7 @@ int tc_threads_i8();
 // passed by value), then the GEMM.
 cudaError_t launch_act_digits(const TcProblem* dev_tab, const TcProblem& single, int count, int rows_max,
                               bool pdl, cudaStream_t s);
-cudaError_t launch_tc_i8(const TcParams& p, const TcPlan& plan, int epi, bool pdl, cudaStream_t s);
+cudaError_t launch_tc_i8(const TcParams& p, const TcPlan& plan, int fmt, int epi, bool pdl, cudaStream_t s);
 
 // ---- dependent-chain decode GEMM: one 128-row tile per cluster (kl_tc_chain.cu)
 // For one int8 row-scale linear with M <= 64 launched after the op that

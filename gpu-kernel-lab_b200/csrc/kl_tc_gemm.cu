@@ -92,9 +92,11 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   TcPlan t{};
   t.ok = false;
   if (units <= 0 || sm_count <= 0) return t;
-  const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM;
+  const bool i8w4 = fmt == kFmtI8W4;
+  const bool w4 = fmt == KL_W4_SYM || fmt == KL_W4_ASYM || i8w4;
   const bool i8 = fmt == kFmtI8;
   if (i8 && !(n_mma == 8 || n_mma == 16 || n_mma == 32 || n_mma == 64)) return t;
+  if (i8w4 && !((n_mma == 8 || n_mma == 16) && kblk == 128)) return t;
   if (!(kblk == 128 || (kblk == 256 && (fmt == KL_W8_ROW || i8) && n_mma <= 64) || (kblk == 256 && w4 && n_mma == 16)))
     return t;
   t.n_mma = n_mma;
@@ -104,15 +106,19 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   // weight stage pitch (the two-group asymmetric 4-bit stages carry their zeros)
   const int wsb = 128 * (w4 ? kblk / 2 : kblk) + ((fmt == KL_W4_ASYM && kblk == 256) ? kZeroStageBytes : 0);
   // x stage: bf16 tiles of n_mma tokens, or (int8 MMA) two digit planes of n_mma tokens
-  const int x_stage = i8 ? (kblk / 128) * i8_tile_rows(n_mma) * 128 : (kblk / 64) * n_mma * 128;
-  const int a_stages = i8 ? 0 : tc_a_stages(n_mma, kblk);
+  const int x_stage = (i8 || i8w4) ? (kblk / 128) * i8_tile_rows(n_mma) * 128 : (kblk / 64) * n_mma * 128;
+  const int a_stages = i8 ? 0 : i8w4 ? 4 : tc_a_stages(n_mma, kblk);
+  const int ndb = i8w4 ? std::min(8, (512 - 4 * (kblk / 4)) / i8_tile_rows(n_mma)) : 2;
   t.x_stages = n_mma == 128 ? 3 : (x_stage > 16384 ? 3 : 4);
+  // digit stages are small and come from L2 (written by the digits pass):
+  // keep about 48 KB of them in flight so that L2 latency does not pace the MMAs
+  if (i8 || i8w4) t.x_stages = std::max(t.x_stages, std::min(12, (48 * 1024) / x_stage));
   // ~128 KB of weights in flight per SM: deeper rings over-subscribe HBM
   const int budget = 220 * 1024;
   int sw = std::max(2, std::min(kMaxWStages, (128 * 1024) / wsb));
-  while (sw > 2 && static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total) > budget) --sw;
+  while (sw > 2 && static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages, ndb).total) > budget) --sw;
   t.w_stages = sw;
-  t.smem = static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages).total);
+  t.smem = static_cast<int>(smem_layout(wsb, x_stage, a_stages, sw, t.x_stages, ndb).total);
   t.workspace = kCounterBytes + static_cast<size_t>(t.grid) * 2 * n_mma * 128 * sizeof(float);
   if (t.grid > kCounterBytes / 4 || t.smem > 227 * 1024) return t;
   t.ok = true;

@@ -63,6 +63,7 @@ struct TcCfg {
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
   static constexpr int D_COL0 = ACOLS * A_STAGES;            // A stages first
   static constexpr int TMEM_COLS = 512;
+  static constexpr int NDB = 2;                              // accumulator buffers
   static_assert(A_STAGES >= 2 && D_COL0 + 2 * NI * D_PITCH <= TMEM_COLS, "TMEM budget");
   // D accumulator of buffer b (0/1) and issuer w
   static constexpr uint32_t d_col(int b, int w) { return D_COL0 + (b * NI + w) * D_PITCH; }
@@ -72,8 +73,11 @@ struct TcCfg {
   static constexpr int X_STAGE = X_ATOMS * X_ATOM;
 };
 
-template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL_W4_ASYM; }
+template <int FMT> constexpr bool is_w4() { return FMT == KL_W4_SYM || FMT == KL_W4_ASYM || FMT == kFmtI8W4; }
 template <int FMT> constexpr bool is_i8() { return FMT == kFmtI8; }
+template <int FMT> constexpr bool is_i8w4() { return FMT == kFmtI8W4; }
+// bf16 group scales and zero points (the asymmetric format's data)
+template <int FMT> constexpr bool asym4() { return FMT == KL_W4_ASYM || FMT == kFmtI8W4; }
 
 // Int8-MMA row format (kFmtI8): the weights are the MMA's A operand straight
 // from the TMA-filled shared-memory stage (int8, K-major, 128B swizzle), and
@@ -92,6 +96,7 @@ struct TcCfgI8 {
   static constexpr int D_COL0 = 0;
   static constexpr int TMEM_COLS = 2 * ROWS <= 32 ? 32 : 2 * ROWS <= 64 ? 64 : 2 * ROWS <= 128 ? 128
                                  : 2 * ROWS <= 256 ? 256 : 512;   // two accumulator buffers, a power of two
+  static constexpr int NDB = 2;
   static constexpr uint32_t d_col(int b, int w) { return D_COL0 + (b * NI + w) * D_PITCH; }
   static constexpr int KSTEPS = KBL / 32;                    // MMAs (K = 32 each) per stage
   static constexpr int X_ATOM = ROWS * 128;                  // bytes: the tile's digit rows x 128
@@ -99,8 +104,41 @@ struct TcCfgI8 {
   static constexpr int X_STAGE = X_ATOMS * X_ATOM;
   static_assert(X_ATOM % 1024 == 0, "digit atoms stay 1024-byte aligned for the 128-byte swizzle");
 };
+// Int8-MMA 4-bit format (kFmtI8W4): the converters turn each 128-group of
+// nibbles into int8 (q - z) -- exact, four per TMEM column -- as the A operand
+// of tcgen05.mma.kind::i8 against the same digit planes as kFmtI8.  Every
+// group is its own accumulation (the epilogue applies its bf16 scale), so the
+// accumulator ring is deep: int8 A stages take half the TMEM of bf16 ones,
+// which leaves room for 8 accumulators and lets the epilogue trail the MMAs
+// by several groups instead of holding them every second stage.
+template <int T, int KBL>
+struct TcCfgI8W4 {
+  static_assert(KBL == 128, "one 128-group per stage");
+  static constexpr int NI = 1;
+  static constexpr int ACOLS = KBL / 4;                      // int8: four per 32-bit column
+  static constexpr int A_STAGES = 4;
+  static constexpr int ROWS = i8_tile_rows(T);
+  static constexpr int D_PITCH = ROWS;
+  static constexpr int D_COL0 = ACOLS * A_STAGES;
+  static constexpr int NDB_FIT = (512 - D_COL0) / D_PITCH;
+  static constexpr int NDB = NDB_FIT > 8 ? 8 : NDB_FIT;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(NDB >= 2, "TMEM budget");
+  static constexpr uint32_t d_col(int b, int w) { return D_COL0 + (b * NI + w) * D_PITCH; }
+  static constexpr int KSTEPS = KBL / 32;                    // MMAs (K = 32 each) per stage
+  static constexpr int X_ATOM = ROWS * 128;
+  static constexpr int X_ATOMS = KBL / 128;
+  static constexpr int X_STAGE = X_ATOMS * X_ATOM;
+};
 template <int FMT, int NMMA, int KBL>
-using TcCfgOf = std::conditional_t<is_i8<FMT>(), TcCfgI8<NMMA, KBL>, TcCfg<NMMA, KBL>>;
+using TcCfgOf = std::conditional_t<is_i8<FMT>(), TcCfgI8<NMMA, KBL>,
+                                   std::conditional_t<is_i8w4<FMT>(), TcCfgI8W4<NMMA, KBL>, TcCfg<NMMA, KBL>>>;
+
+// s * (65536 h + 256 m + l) from the three int32 digit-plane sums, one rounding
+KL_DEVICE float digits3(uint32_t h, uint32_t m, uint32_t l) {
+  return fmaf(65536.0f, static_cast<float>(static_cast<int>(h)),
+              fmaf(256.0f, static_cast<float>(static_cast<int>(m)), static_cast<float>(static_cast<int>(l))));
+}
 
 // Warp roles: 0 W-TMA, 1 MMA issuer 0 (+ TMEM owner), 2 X-TMA, then CW
 // converter warps (CW/4 per TMEM lane quadrant, each converting a 1/(CW/4)
@@ -121,7 +159,10 @@ struct TcRoles {
   static constexpr int NI = TcCfgOf<FMT, NMMA, KBL>::NI;
   static constexpr int CW = is_i8<FMT>() ? 0
                           : (KBL == 256 && NMMA == 16 && !(FMT == KL_W4_SYM || FMT == KL_W4_ASYM)) ? 16 : 8;
-  static constexpr int CG = (KBL == 256 && NMMA == 16 && (FMT == KL_W4_SYM || FMT == KL_W4_ASYM)) ? 2 : 1;
+  // two converter groups on alternate units: two-group 4-bit stages, and the
+  // int8 4-bit format (a thread converts a whole 128-wide row per unit)
+  static constexpr int CG = (is_i8w4<FMT>() || (KBL == 256 && NMMA == 16 && (FMT == KL_W4_SYM || FMT == KL_W4_ASYM)))
+                                ? 2 : 1;
   static constexpr int CWG = is_i8<FMT>() ? 4 : CW / CG;    // converter warps per group (per unit)
   static constexpr int CONV0 = 3;
   static constexpr int EPI0_WARP0 = CONV0 + CW;
@@ -155,7 +196,7 @@ constexpr int kUnitCacheBytes = 8 * kMaxGroup;    // problem unit_begin cache (g
 struct SmemLayout {
   uint32_t w, x, xch, ucache, zoff, bars, misc, total;
 };
-__host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a_stages, int sw, int sx) {
+__host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a_stages, int sw, int sx, int ndb = 2) {
   SmemLayout l{};
   l.w = 0;
   l.x = l.w + sw * wsb;
@@ -163,8 +204,8 @@ __host__ __device__ constexpr SmemLayout smem_layout(int wsb, int x_stage, int a
   l.ucache = l.xch + kXchBytes;
   l.zoff = l.ucache + kUnitCacheBytes;       // per weight stage: zero-point offset in its box (4 B each)
   l.bars = l.zoff + 4 * kMaxWStages;
-  // w_full, w_empty [sw]; x_full, x_empty [sx]; a_full, a_empty [A]; d_full, d_empty [2]; done
-  l.misc = l.bars + 8 * (2 * sw + 2 * sx + 2 * a_stages + 5);
+  // w_full, w_empty [sw]; x_full, x_empty [sx]; a_full, a_empty [A]; d_full, d_empty [ndb]; done
+  l.misc = l.bars + 8 * (2 * sw + 2 * sx + 2 * a_stages + 2 * ndb + 1);
   l.total = l.misc + 16 + 1024;           // + slack to align the base to 1024 B
   return l;
 }
@@ -477,6 +518,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   constexpr bool SWIGLU = EPI == kEpiSwiglu;
   using Cfg = TcCfgOf<FMT, NMMA, KBL>;
   constexpr bool I8 = is_i8<FMT>();
+  constexpr bool DIG = is_i8<FMT>() || is_i8w4<FMT>();   // B operand = activation digit planes
   using Roles = TcRoles<FMT, NMMA, KBL>;
   using E = Epi<FMT, NMMA, EPI, XBF16>;
   static_assert(!grouped<FMT>() || KBL == 128 || (KBL == 256 && NMMA == 16), "4-bit group mode: one or two groups of 128 per stage");
@@ -492,7 +534,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int SW = p.w_stages, SX = p.x_stages;
-  const SmemLayout L = smem_layout(WSP, Cfg::X_STAGE, A, SW, SX);
+  constexpr int NDB = Cfg::NDB;
+  const SmemLayout L = smem_layout(WSP, Cfg::X_STAGE, A, SW, SX, NDB);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t s_w = s_base + L.w, s_x = s_base + L.x, s_bars = s_base + L.bars;
   float* xch = reinterpret_cast<float*>(smem + L.xch);
@@ -508,8 +551,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
   auto a_full = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + i); };
   auto a_empty = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + A + i); };
   auto d_full = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + 2 * A + i); };
-  auto d_empty = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + 2 * A + 2 + i); };
-  const uint32_t done_bar = s_bars + 8u * (2 * SW + 2 * SX + 2 * A + 4);
+  auto d_empty = [&](int i) { return s_bars + 8u * (2 * SW + 2 * SX + 2 * A + NDB + i); };
+  const uint32_t done_bar = s_bars + 8u * (2 * SW + 2 * SX + 2 * A + 2 * NDB);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long G = gridDim.x, c = blockIdx.x;
@@ -553,7 +596,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     for (int i = 0; i < SW; ++i) { mbar_init(w_full(i), 1); mbar_init(w_empty(i), I8 ? Cfg::NI : Roles::CWG); }
     for (int i = 0; i < SX; ++i) { mbar_init(x_full(i), 1); mbar_init(x_empty(i), Cfg::NI); }
     for (int i = 0; i < A; ++i) { mbar_init(a_full(i), Roles::CWG); mbar_init(a_empty(i), Cfg::NI); }
-    for (int i = 0; i < 2; ++i) { mbar_init(d_full(i), Cfg::NI); mbar_init(d_empty(i), 4); }
+    for (int i = 0; i < NDB; ++i) { mbar_init(d_full(i), Cfg::NI); mbar_init(d_empty(i), 4); }
     mbar_init(done_bar, Cfg::NI);
     *abort_flag = 0;
     fix_flags[0] = 0;
@@ -605,8 +648,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         mbar_arrive_expect_tx(x_full(px.idx), Cfg::X_STAGE);
 #pragma unroll
         for (int a = 0; a < Cfg::X_ATOMS; ++a)
-          tma_load_2d(dst + a * Cfg::X_ATOM, &pr.tmap_x, cx.kb * KBL + (I8 ? 128 : 64) * a,
-                      cx.mt * (I8 ? i8_tile_rows(NMMA) : NMMA), x_full(px.idx));
+          tma_load_2d(dst + a * Cfg::X_ATOM, &pr.tmap_x, cx.kb * KBL + (DIG ? 128 : 64) * a,
+                      cx.mt * (DIG ? i8_tile_rows(NMMA) : NMMA), x_full(px.idx));
         px.next();
         ++issued;
       }
@@ -623,7 +666,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       constexpr int NBLK_W = KBL / 128;
       static_assert(Cfg::KSTEPS == 4 * NBLK_W, "four K = 32 steps per 128-byte column block");
       const uint32_t w_desc0 = smem_desc_sw128_lo(s_w), x_desc0 = smem_desc_sw128_lo(s_x);
-      Pipe pwm{0, SW, 0}, px{0, SX, 0}, pd{0, 2, 0};
+      Pipe pwm{0, SW, 0}, px{0, SX, 0}, pd{0, NDB, 0};
       bool ok = true;
       Cursor cm;
       cm.init(probs, u_lo, u_hi);
@@ -656,8 +699,8 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       __syncwarp();
       mbar_wait_time(done_bar, 0);
     } else {
-      constexpr uint32_t idesc = make_idesc_f16(128, NMMA, XBF16);
-      constexpr int JPER = Cfg::KSTEPS / Cfg::NI;    // K steps of 16 per issuer and stage
+      constexpr uint32_t idesc = is_i8w4<FMT>() ? make_idesc_i8(128, i8_tile_rows(NMMA)) : make_idesc_f16(128, NMMA, XBF16);
+      constexpr int JPER = Cfg::KSTEPS / Cfg::NI;    // K steps (of 16, or 32 for int8) per issuer and stage
       const int w = warp == 1 ? 0 : warp - Roles::ISS1_WARP0 + 1;
       // Descriptor and TMEM offsets of this issuer's K steps, computed once:
       // the issue loop then costs one add per operand per MMA.
@@ -669,7 +712,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         b_off[jj] = static_cast<uint32_t>((j >> 2) * Cfg::X_ATOM + (j & 3) * 32) >> 4;
       }
       const uint32_t a_off = 8u * static_cast<uint32_t>(w * JPER);
-      Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, 2, 0};
+      Pipe px{0, SX, 0}, pa{0, A, 0}, pd{0, NDB, 0};
       bool ok = true;
       Cursor cm;
       cm.init(probs, u_lo, u_hi);
@@ -685,8 +728,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         const uint32_t xd = x_desc0 + static_cast<uint32_t>(px.idx * (Cfg::X_STAGE >> 4));
         if (elect_one()) {
 #pragma unroll
-          for (int jj = 0; jj < JPER; ++jj)
-            tc_mma_ts_lo(d_tmem, a_tmem + 8u * jj, xd + b_off[jj], idesc, (chunk_start && jj == 0) ? 0u : 1u);
+          for (int jj = 0; jj < JPER; ++jj) {
+            if constexpr (is_i8w4<FMT>())
+              tc_mma_ts_i8_lo(d_tmem, a_tmem + 8u * jj, xd + b_off[jj], idesc, (chunk_start && jj == 0) ? 0u : 1u);
+            else
+              tc_mma_ts_lo(d_tmem, a_tmem + 8u * jj, xd + b_off[jj], idesc, (chunk_start && jj == 0) ? 0u : 1u);
+          }
           tc_commit(x_empty(px.idx));
           tc_commit(a_empty(pa.idx));
           if (chunk_end) tc_commit(d_full(pd.idx));
@@ -724,7 +771,7 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     // 4-bit zero point of this thread's row for a unit (a global load, issued
     // one unit ahead so its latency overlaps the previous unit's conversion)
     auto load_zero = [&](const Cursor& cu) -> float {
-      if constexpr (FMT == KL_W4_ASYM) {
+      if constexpr (asym4<FMT>()) {
         const TcProblem& pz = *cu.pr;
         int zr = E::phys_row(pz, cu.nt, r);
         zr = zr < pz.n ? zr : pz.n - 1;
@@ -788,6 +835,39 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
           }
           tmem_st16(a_tmem + 16u * j, part);
         }
+      } else if constexpr (is_i8w4<FMT>()) {
+        // EPT nibbles of row r = EPT/32 chunks of 16 B (64B swizzle: chunk g at
+        // g ^ ((r >> 1) & 3)) -> EPT int8 (q - z) in K order, EPT/4 TMEM columns.
+        // Per 8 nibbles: the even and odd codes as bytes 128 + c (one lop3
+        // each), interleaved back into K order (two byte permutes), minus z in
+        // every byte (no borrow: 128 + c - z >= 113), then ^ 0x80 leaves the
+        // two's-complement int8 q - z.
+        static_assert(EPT % 64 == 0, "whole 16-column TMEM stores");
+        const uint32_t z4 = static_cast<uint32_t>(__float2int_rn(zg0)) * 0x01010101u;
+        uint4 v[EPT / 32];
+#pragma unroll
+        for (int cc = 0; cc < EPT / 32; ++cc) {
+          const int g = h * (EPT / 32) + cc;
+          v[cc] = *reinterpret_cast<const uint4*>(wstage + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+        }
+#pragma unroll
+        for (int c2 = 0; c2 < EPT / 64; ++c2) {
+          uint32_t part[16];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t wd[4] = {v[2 * c2 + c].x, v[2 * c2 + c].y, v[2 * c2 + c].z, v[2 * c2 + c].w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const uint32_t lo = lop3<0xEA>(wd[t], 0x0F0F0F0Fu, 0x80808080u);
+              const uint32_t hi = lop3<0xEA>(wd[t] >> 4, 0x0F0F0F0Fu, 0x80808080u);
+              part[c * 8 + 2 * t] = (prmt(lo, hi, 0x5140u) - z4) ^ 0x80808080u;
+              part[c * 8 + 2 * t + 1] = (prmt(lo, hi, 0x7362u) - z4) ^ 0x80808080u;
+            }
+          }
+          tmem_st16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(Cfg::ACOLS) * pa.idx +
+                        static_cast<uint32_t>(EPT / 4) * h + 16u * c2,
+                    part);
+        }
       } else {
         // EPT nibbles = EPT/32 chunks of 16 B; 64B swizzle: chunk g at g ^ ((r >> 1) & 3)
         auto bias_of = [&](float z) {
@@ -843,9 +923,10 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     pdl_wait();                             // outputs / workspace written only after the previous kernel
     // chunk c uses accumulator buffer c % 2; with two groups, group g takes the
     // chunks with c % 2 == g, i.e. always buffer g
-    Pipe pd{eg, 2, 0};
+    Pipe pd{eg, NDB, 0};
     int chunk = 0;
-    float acc[grouped<FMT>() ? NMMA : 1];
+    constexpr int NCHG = (NMMA + 15) / 16;   // 16-column chunks of a token tile
+    float acc[grouped<FMT>() ? NCHG * 16 : 1];
     int seg_kb0 = 0;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // 16 columns of the accumulator: the sum of the NI issuers' partial D regions
@@ -876,16 +957,44 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
     Cursor ce;
     ce.init(probs, u_lo, u_hi);
     const long long first_tile_u0 = ce.tile_u0;
+    // int8 4-bit format: every unit is one group whose scale the epilogue needs
+    // right after the accumulator wait; a cursor running kAhead units ahead
+    // loads the scales early (a ring in registers) so that their latency is
+    // not paid once per unit
+    constexpr int kAhead = is_i8w4<FMT>() ? 3 : 0;
+    float gring[kAhead + 1];
+    Cursor cs = ce;
+    auto scale_at = [&](const Cursor& cu) -> float {
+      const TcProblem& pz = *cu.pr;
+      int zr = E::phys_row(pz, cu.nt, r);
+      zr = zr < pz.n ? zr : pz.n - 1;
+      return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pz.scales)[static_cast<long long>(zr) * cu.kb_total + cu.kb]);
+    };
+    if constexpr (kAhead > 0) {
+#pragma unroll
+      for (int a = 0; a < kAhead; ++a) {
+        gring[a] = a < n_local ? scale_at(cs) : 0.0f;
+        if (a < n_local) cs.next();
+      }
+    }
     bool ok = true;
     for (int i = 0; i < n_local && ok; ++i, ce.next()) {
       const TcProblem& pr = *ce.pr;
       const int mt = ce.mt, nt = ce.nt;
+      float g_cur = 1.0f;
+      if constexpr (kAhead > 0) {
+        gring[kAhead] = i + kAhead < n_local ? scale_at(cs) : 0.0f;
+        if (i + kAhead < n_local) cs.next();
+        g_cur = gring[0];
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) gring[a] = gring[a + 1];
+      }
       const bool seg_end = ce.seg_end();
       if (ce.seg_start()) {
         seg_kb0 = ce.kb;
         if constexpr (grouped<FMT>()) {
 #pragma unroll
-          for (int j = 0; j < NMMA; ++j) acc[j] = 0.f;
+          for (int j = 0; j < NCHG * 16; ++j) acc[j] = 0.f;
         }
       }
       const bool chunk_end = grouped<FMT>() ? true : seg_end;
@@ -897,12 +1006,14 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
       float gs[GPS];                           // group scales, loaded before the wait
 #pragma unroll
       for (int gi = 0; gi < GPS; ++gi) gs[gi] = 1.0f;
-      if constexpr (grouped<FMT>()) {
+      if constexpr (is_i8w4<FMT>()) {
+        gs[0] = g_cur;
+      } else if constexpr (grouped<FMT>()) {
         const int pr_row = prow < pr.n ? prow : pr.n - 1;
         const long long sbase = static_cast<long long>(pr_row) * ce.kb_total * GPS + ce.kb * GPS;
 #pragma unroll
         for (int gi = 0; gi < GPS; ++gi) {
-          if constexpr (FMT == KL_W4_ASYM)
+          if constexpr (asym4<FMT>())
             gs[gi] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(pr.scales)[sbase + gi]);
           else
             gs[gi] = reinterpret_cast<const float*>(pr.scales)[sbase + gi];
@@ -919,7 +1030,30 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         part_base = p.partials + (c * 2 + slot) * static_cast<long long>(NMMA) * 128;
       }
       if constexpr (grouped<FMT>()) {
-        if constexpr (GPS == 1) {
+        if constexpr (is_i8w4<FMT>()) {
+          // the group's three int32 digit sums -> f32 times the group scale; the
+          // token scales (one per tile) are applied where the tile is finished
+          const float s = gs[0];
+          if constexpr (NMMA == 8) {
+            uint32_t t0[16], t1[16];             // columns 0-7 h, 8-15 m, 16-23 l
+            tmem_ld16(d_tmem, t0);
+            tmem_ld16(d_tmem + 16u, t1);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(s, digits3(t0[j], t0[8 + j], t1[j]), acc[j]);
+          } else {
+#pragma unroll
+            for (int cb = 0; cb < NMMA / 16; ++cb) {
+              uint32_t th[16], tm[16], tl[16];
+              tmem_ld16(d_tmem + 16u * cb, th);
+              tmem_ld16(d_tmem + static_cast<uint32_t>(NMMA) + 16u * cb, tm);
+              tmem_ld16(d_tmem + static_cast<uint32_t>(2 * NMMA) + 16u * cb, tl);
+              tc_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[cb * 16 + j] = fmaf(s, digits3(th[j], tm[j], tl[j]), acc[cb * 16 + j]);
+            }
+          }
+        } else if constexpr (GPS == 1) {
           const float s = gs[0];
 #pragma unroll
           for (int cb = 0; cb < NMMA / 16; ++cb) {
@@ -947,9 +1081,14 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
         if (lane == 0) mbar_arrive(d_empty(pd.idx));
         if (Roles::EPI_GROUPS == 2) pd.phase ^= 1u; else pd.next();
         if (!seg_end) continue;
+        if constexpr (is_i8w4<FMT>()) {
+          const float* tsp = pr.tscale + static_cast<long long>(mt) * NMMA;
+#pragma unroll
+          for (int j = 0; j < NMMA; ++j) acc[j] *= tsp[j];
+        }
         if (full_tile) {
 #pragma unroll
-          for (int cb = 0; cb < NMMA / 16; ++cb) {
+          for (int cb = 0; cb < NCHG; ++cb) {
             float o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = acc[cb * 16 + j];
@@ -957,11 +1096,12 @@ tc_qgemm_kernel(const __grid_constant__ TcParams p) {
           }
           continue;
         }
+        const int mvg = min(mrem, NMMA);
 #pragma unroll
-        for (int cb = 0; cb < NMMA / 16; ++cb)
+        for (int cb = 0; cb < NCHG; ++cb)
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (cb * 16 + j < mrem) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
+            if (cb * 16 + j < mvg) part_base[(cb * 16 + j) * 128 + r] = acc[cb * 16 + j];
       } else if constexpr (I8) {
         // int32 digit sums -> f32: v = s_t * (65536 h + 256 m + l) per token
         // (s_t a power of two, so the only roundings are the two f32 adds); the

@@ -1,5 +1,6 @@
 // Int8 tensor-core mode of the persistent weight-only GEMM for int8 row-scale
-// weights (KL_W8_ROW), used by grouped decode launches.
+// weights (KL_W8_ROW) and asymmetric 4-bit group-128 weights (KL_W4_ASYM),
+// used by grouped decode launches.
 //
 // The bf16 path converts every weight to bf16 on the CUDA cores before the
 // MMA; at decode sizes that conversion, not HBM, sets the pace, and under the
@@ -157,6 +158,17 @@ cudaError_t launch_tokens(const TcParams& p, const TcPlan& plan, bool pdl, cudaS
   }
 }
 
+// 4-bit asymmetric weights: one 128-group per stage, token tiles of 8 or 16
+template <int EPI>
+cudaError_t launch_tokens_w4(const TcParams& p, const TcPlan& plan, bool pdl, cudaStream_t s) {
+  if (plan.kblk != 128) return cudaErrorInvalidValue;
+  switch (plan.n_mma) {
+    case 8: return launch_one<kFmtI8W4, 8, 128, EPI, true>(p, plan, pdl, s);
+    case 16: return launch_one<kFmtI8W4, 16, 128, EPI, true>(p, plan, pdl, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
 
 int tc_choose_tokens_i8(int m) { return m <= 8 ? 8 : m <= 16 ? 16 : m <= 32 ? 32 : 64; }
@@ -179,7 +191,13 @@ cudaError_t launch_act_digits(const TcProblem* dev_tab, const TcProblem& single,
   return cudaLaunchKernelEx(&cfg, act_digits_kernel, count > 1 ? dev_tab : nullptr, single);
 }
 
-cudaError_t launch_tc_i8(const TcParams& p, const TcPlan& plan, int epi, bool pdl, cudaStream_t s) {
+cudaError_t launch_tc_i8(const TcParams& p, const TcPlan& plan, int fmt, int epi, bool pdl, cudaStream_t s) {
+  if (fmt == kFmtI8W4) {
+    if (epi == kEpiSwiglu) return launch_tokens_w4<kEpiSwiglu>(p, plan, pdl, s);
+    if (epi == kEpiPlain) return launch_tokens_w4<kEpiPlain>(p, plan, pdl, s);
+    return cudaErrorInvalidValue;
+  }
+  if (fmt != kFmtI8) return cudaErrorInvalidValue;
   if (epi == kEpiSwiglu) return launch_tokens<kEpiSwiglu>(p, plan, pdl, s);
   if (epi == kEpiPlain) return launch_tokens<kEpiPlain>(p, plan, pdl, s);
   return cudaErrorInvalidValue;

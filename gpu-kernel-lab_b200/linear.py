@@ -205,8 +205,12 @@ class GroupedLinear:
     Groups whose every problem has at least 256 tokens (int8 row weights,
     K a multiple of 64) run on the CTA-pair prefill kernel instead, the tiles
     of all problems in one launch (unless ``mma="int8"``).
-    ``"auto"`` (default) takes ``"int8"`` for int8 row weights with bf16
-    activations and at most 8 tokens per problem, else ``"bf16"``: the three
+    For asymmetric 4-bit group-128 weights (at most 16 tokens) the int8 mode
+    converts each nibble to the int8 ``q - z`` instead of bf16; it measured
+    slower than the bf16 mode on the config 3 set (157-164 against 101 us), so
+    ``"auto"`` does not take it.
+    ``"auto"`` (default) takes ``"int8"`` for bf16 activations with int8 row
+    weights and at most 8 tokens per problem, else ``"bf16"``: the three
     digit planes make the int8 MMA 3 tokens wide per token, which costs more
     tensor time than the bf16 conversion saves once tiles are 16 tokens or
     wider (measured on the config 1 set: 101 against 108 us at M = 1, 163

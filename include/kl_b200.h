@@ -141,9 +141,11 @@ int kl_linear_grouped(const void* host_table, const void* device_table, void* wo
                       size_t workspace_bytes, int flags, void* stream);
 
 /*
- * Int8 tensor-core mode of the grouped launch (KL_W8_ROW weights, bf16
- * activations).  No reference counterpart: the same computation as the
- * default mode, with the weights fed to tcgen05.mma.kind::i8 unconverted.
+ * Int8 tensor-core mode of the grouped launch (bf16 activations; KL_W8_ROW
+ * weights, or KL_W4_ASYM weights with group 128 and m <= 16).  No reference
+ * counterpart: the same computation as the default mode, with int8 weights fed
+ * to tcgen05.mma.kind::i8 unconverted (4-bit codes become the exact int8
+ * q - z).
  * kl_linear_grouped then runs two kernels on the stream: a digits pass that
  * writes every token row as a power-of-two scale s_t = 2^(floor(log2 max|x|) - 21)
  * and three int8 planes h, m, l with x = s_t * (65536 h + 256 m + l) (exact

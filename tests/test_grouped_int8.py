@@ -164,8 +164,11 @@ def test_int8_mode_graph_replay_and_new_inputs():
 
 
 def test_int8_mode_rejects_other_formats():
+    """The int8 mode takes int8 row weights and asymmetric 4-bit group-128
+    weights with bf16 activations; the symmetric 4-bit format and f16
+    activations are rejected."""
     x, w = make(1, 256, 256, seed=1)
-    p = kl.quantize_int4_asym(w.cuda(), 128)
+    p = kl.quantize_int4(w.cuda(), 128)
     with pytest.raises(Exception):
         kl.GroupedLinear([(x.cuda(), p, torch.empty(1, 256, device="cuda", dtype=torch.bfloat16))], mma="int8")
     p8, _, _ = quantize(w)

@@ -105,3 +105,50 @@ def test_w4_grouped(m):
     torch.cuda.synchronize()
     for (_, p, y), (rows, ref) in zip(probs, refs):
         assert_matches_oracle(y[:, torch.from_numpy(rows).cuda()], ref, what=f"w4 grouped m={m}")
+
+
+@pytest.mark.parametrize("mma", ["int8", "bf16"])
+@pytest.mark.parametrize("m", [1, 5, 9, 16])
+def test_w4_grouped_modes(m, mma):
+    """Both tensor-core modes of the grouped 4-bit launch: int8 (q - z) against
+    the activation digit planes (token tiles of 8 and 16) and bf16 (q - z)."""
+    shapes = [(4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (200, 256)]
+    probs, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        x, w = make(m, n, k, seed=70 + i + m)
+        p, d, s, z = quantize_asym(w)
+        probs.append((x.cuda(), p, torch.empty(m, n, device="cuda", dtype=torch.bfloat16)))
+        refs.append(O.linear_f32(x.float().numpy(), O.dequantize_int4_asym(d, s, z, 128)))
+    g = kl.GroupedLinear(probs, mma=mma)
+    assert g.mma == mma
+    g.run()
+    torch.cuda.synchronize()
+    assert kl._native.device_status(torch.cuda.current_device()) == 0
+    for (_, p, y), ref in zip(probs, refs):
+        assert_matches_oracle(y, ref, what=f"w4 grouped {mma} {tuple(p.data.shape)} m={m}")
+
+
+def test_w4_grouped_int8_swiglu_and_replay():
+    m, n, k = 16, 6144, 1024
+    probs, refs = [], []
+    for i in range(2):
+        x, w = make(m, n, k, seed=90 + i)
+        p, d, s, z = quantize_asym(w)
+        probs.append((x.cuda(), p, torch.empty(m, n // 2, device="cuda", dtype=torch.bfloat16)))
+        refs.append(O.swiglu(O.bf16_round(O.linear_f32(x.float().numpy(), O.dequantize_int4_asym(d, s, z, 128)))))
+    g = kl.GroupedLinear(probs, swiglu=True, mma="int8")
+    assert g.mma == "int8"
+    g.run()
+    torch.cuda.synchronize()
+    for (_, _, y), ref in zip(probs, refs):
+        assert_matches_oracle(y, ref, what="w4 int8 swiglu")
+    first = [y.clone() for _, _, y in probs]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        g.run(pdl=True)
+    for _, _, y in probs:
+        y.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, (_, _, y) in zip(first, probs):
+        assert torch.equal(a, y)
