@@ -859,8 +859,27 @@ def bench_prefill(args, kl, world, rank, local, dist):
     hbm, tf_burst, tf_sus, peak_kind = measured_peaks()
     res = {}
     total_flops, total_ms = 0.0, 0.0
+    grouped = {}
     with ClockSampler(local) as clocks:
         for m in ms_list:
+            # the 28 layers' GEMMs with independent activations as ONE grouped
+            # CTA-pair launch (the first tc_prefill launches of the run: one
+            # eager call, then the graph replays)
+            probs = []
+            for _ in range(LAYERS):
+                for name, p, sw in weights:
+                    n, k = p.data.shape
+                    probs.append((torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16), p,
+                                  torch.empty(m, n // 2 if sw else n, device=device, dtype=torch.bfloat16)))
+            grp = kl.GroupedLinear(probs, swiglu=bool(args.swiglu))
+            grp.run(pdl=True)
+            torch.cuda.synchronize()
+            gg = capture(lambda: grp.run(pdl=True))
+            gms = max_over_ranks(timed(gg, args.steps, warm=args.warmup), dist, device)
+            gflops = sum(2 * m * p.data.shape[0] * p.data.shape[1] for _, p, _ in probs)
+            grouped[str(m)] = {"ms": round(gms, 4), "TFLOP/s": round(gflops / (gms * 1e-3) / 1e12, 1),
+                               "frac": round(gflops / (gms * 1e-3) / 1e12 / tf_burst, 3)}
+            del gg, grp, probs
             items = []
             for name, p, sw in weights:
                 n, k = p.data.shape
@@ -901,7 +920,7 @@ def bench_prefill(args, kl, world, rank, local, dist):
             "config": {"workload": "qwen3-0.6b prefill layer GEMMs (BASELINE config 2)", "batch_m": ms_list,
                        "swiglu": bool(args.swiglu), "launch": "the 4 layer GEMMs of each M as one CUDA graph, programmatic dependent launch",
                        "l2": "no flush: at M>=2048 each graph replay streams more than the 126 MB L2 in activations and outputs"},
-            "per_m": res,
+            "per_m": res, "grouped_per_m": grouped,
             "roofline": {"bound": "tensor", "achieved": round(value / world, 1), "peak": tf_burst, "unit": "TFLOP/s",
                          "frac": round(value / world / tf_burst, 4), "peak_source": peak_kind, "traffic": None},
             "gpu_launches": len(weights) * len(ms_list) * args.steps,
