@@ -107,8 +107,9 @@ TcPlan plan_tc(int n_mma, int kblk, long long units, int fmt, int sm_count) {
   const int wsb = 128 * (w4 ? kblk / 2 : kblk) + ((fmt == KL_W4_ASYM && kblk == 256) ? kZeroStageBytes : 0);
   // x stage: bf16 tiles of n_mma tokens, or (int8 MMA) two digit planes of n_mma tokens
   const int x_stage = (i8 || i8w4) ? (kblk / 128) * i8_tile_rows(n_mma) * 128 : (kblk / 64) * n_mma * 128;
-  const int a_stages = i8 ? 0 : i8w4 ? 4 : tc_a_stages(n_mma, kblk);
-  const int ndb = i8w4 ? std::min(8, (512 - 4 * (kblk / 4)) / i8_tile_rows(n_mma)) : 2;
+  const bool w4_pair = (fmt == KL_W4_SYM || fmt == KL_W4_ASYM) && kblk == 256 && n_mma == 16;
+  const int a_stages = i8 ? 0 : i8w4 ? 4 : w4_pair ? 2 : tc_a_stages(n_mma, kblk);
+  const int ndb = i8w4 ? std::min(8, (512 - 4 * (kblk / 4)) / i8_tile_rows(n_mma)) : w4_pair ? 4 : 2;
   t.x_stages = n_mma == 128 ? 3 : (x_stage > 16384 ? 3 : 4);
   // digit stages are small and come from L2 (written by the digits pass):
   // keep about 48 KB of them in flight so that L2 latency does not pace the MMAs

@@ -130,9 +130,27 @@ struct TcCfgI8W4 {
   static constexpr int X_ATOMS = KBL / 128;
   static constexpr int X_STAGE = X_ATOMS * X_ATOM;
 };
+// Two-group bf16 4-bit stages (K block 256, 16-token tiles): every stage is two
+// accumulations that the epilogue must scale before the MMA may reuse their
+// buffer, so the ring trades one of the three A stages for two more
+// accumulator buffers (2 x 128 A columns + 4 x 64 D columns).
+template <int NMMA, int KBL>
+struct TcCfgW4Pair : TcCfg<NMMA, KBL> {
+  static constexpr int A_STAGES = 2;
+  static constexpr int D_COL0 = TcCfg<NMMA, KBL>::ACOLS * A_STAGES;
+  static constexpr int NDB = 4;
+  static_assert(D_COL0 + NDB * TcCfg<NMMA, KBL>::NI * TcCfg<NMMA, KBL>::D_PITCH <= 512, "TMEM budget");
+  static constexpr uint32_t d_col(int b, int w) {
+    return D_COL0 + (b * TcCfg<NMMA, KBL>::NI + w) * TcCfg<NMMA, KBL>::D_PITCH;
+  }
+};
 template <int FMT, int NMMA, int KBL>
-using TcCfgOf = std::conditional_t<is_i8<FMT>(), TcCfgI8<NMMA, KBL>,
-                                   std::conditional_t<is_i8w4<FMT>(), TcCfgI8W4<NMMA, KBL>, TcCfg<NMMA, KBL>>>;
+constexpr bool w4_pair_stage() { return (FMT == KL_W4_SYM || FMT == KL_W4_ASYM) && KBL == 256 && NMMA == 16; }
+template <int FMT, int NMMA, int KBL>
+using TcCfgOf = std::conditional_t<
+    is_i8<FMT>(), TcCfgI8<NMMA, KBL>,
+    std::conditional_t<is_i8w4<FMT>(), TcCfgI8W4<NMMA, KBL>,
+                       std::conditional_t<w4_pair_stage<FMT, NMMA, KBL>(), TcCfgW4Pair<NMMA, KBL>, TcCfg<NMMA, KBL>>>>;
 
 // s * (65536 h + 256 m + l) from the three int32 digit-plane sums, one rounding
 KL_DEVICE float digits3(uint32_t h, uint32_t m, uint32_t l) {
