@@ -12,6 +12,7 @@
 // array's name is only a host-side stand-in, not a device address, so the
 // device address is looked up with cudaGetSymbolAddress once per device, with
 // that device current, and that address is what the kernel receives.
+#include <algorithm>
 #include <mutex>
 
 #include "kl_common.cuh"
@@ -26,11 +27,13 @@ static_assert(KL_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[KL_NOALLOC_SCRATCH_BYTES];
 
 void* g_scratch_addr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
 std::mutex g_scratch_mutex;
 
-// Device address of this device's scratch array, looked up on the first call
-// made with the device current.
-int scratch_address(void** out) {
+// Device address of this device's scratch array (and its SM count), looked up
+// on the first call made with the device current.  The address stays valid for
+// the life of the device's primary context.
+int scratch_address(void** out, int* sm_count) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return report_error(KL_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
@@ -41,9 +44,15 @@ int scratch_address(void** out) {
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess)
       return report_error(KL_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    int sm = 0;
+    e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess || sm <= 0)
+      return report_error(KL_ERR_CUDA, "cudaDeviceGetAttribute(SM count): %s", cudaGetErrorString(e));
+    g_sm_count[dev] = sm;
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];
+  *sm_count = g_sm_count[dev];
   return KL_OK;
 }
 
@@ -63,14 +72,17 @@ extern "C" int kl_linear_noalloc(const void* x, int x_dtype, int m, int k, const
     return report_error(KL_ERR_WORKSPACE, "kl_linear_noalloc: this problem needs %zu bytes of scratch, the static "
                         "scratch holds %d bytes (device has too many SMs)", need, KL_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
-  int rc = scratch_address(&scratch);
+  int sm_count = 0;
+  int rc = scratch_address(&scratch, &sm_count);
   if (rc != KL_OK) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (need > 0) {
-    // The arrival counters (the first kCounterBytes) must be zero at launch.
+    // The arrival counters at the start of the scratch must be zero at launch.
     // A finished launch leaves them zero, but one that gave up on a timed-out
-    // wait may not, so clear them on the caller's stream every time.
-    const cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, s);
+    // wait may not, so clear them on the caller's stream every time: one per
+    // CTA of a stream-K grid, which has at most one CTA per SM.
+    const size_t used = std::min<size_t>(kCounterBytes, (static_cast<size_t>(sm_count) * sizeof(int) + 255) & ~size_t(255));
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, used, s);
     if (e != cudaSuccess) return report_error(KL_ERR_CUDA, "cudaMemsetAsync(scratch counters): %s", cudaGetErrorString(e));
   }
   return kl_linear(x, x_dtype, m, k, w, KL_W8_ROW, n, k, scales, nullptr, nullptr, swiglu, y,

@@ -99,8 +99,9 @@ size_t kl_linear_workspace_bytes(int m, int n, int k, int w_format, int swiglu, 
  *     library, held on every GPU that loads it until the process exits.  Enough
  *     for m <= KL_NOALLOC_MAX_M on devices with up to 160 SMs; larger m returns
  *     KL_ERR_INVALID, a device whose plan needs more returns KL_ERR_WORKSPACE.
- *   The first call on each device looks up that device's scratch address; make
- *     that first call before any stream capture.
+ *   The first call on each device looks up that device's scratch address (valid
+ *     for the life of the device's primary context; a cudaDeviceReset ends it);
+ *     make that first call before any stream capture.
  *   Every call clears the scratch's arrival counters on `stream` before the
  *     kernel.  All calls share the one array, so calls that overlap on the GPU
  *     (two streams, two host threads) race; keep them ordered on one stream.
