@@ -278,7 +278,7 @@ int kl_linear(const void* x, int x_dtype, int m, int k, const void* w, int w_for
     p.vec_store = (aligned16(y) && p.ldy % 8 == 0) ? (transposed ? 2 : 1) : 0;
     p.status = di.status;
     prefill_tiles(p, swiglu != 0, di.sm_count);
-    rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != KL_OK) return rc;
     // each CTA of a pair loads half of the tile's tokens
     rc = encode_2d(&p.tmap_x, xbf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, k, m,
@@ -530,7 +530,7 @@ int kl_grouped_encode_ex(const kl_problem* problems, int count, int x_dtype, int
     for (int i = 0; i < count; ++i) {
       const kl_problem& q = problems[i];
       PfParams& p = tab[i];
-      int rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.w, q.k, q.n, q.k, 64, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+      int rc = encode_2d(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.w, q.k, q.n, q.k, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
       if (rc != KL_OK) return rc;
       rc = encode_2d(&p.tmap_x, x_dtype == KL_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                      q.x, q.k, q.m, static_cast<uint64_t>(q.k) * act_bytes(x_dtype), 64,

@@ -182,7 +182,7 @@ cudaError_t launch_gemv_chain(const GemvChainParams& p, const GemvChainPlan& pla
 // ---- prefill: int8 row-scale GEMM on CTA pairs (kl_tc_prefill.cu)
 constexpr int kPrefillMinM = 256;     // token count from which kl_linear uses the pair kernel
 struct PfParams {
-  CUtensorMap tmap_w;                 // int8 [N, K], box 64 x 64 rows, 64B swizzle
+  CUtensorMap tmap_w;                 // int8 [N, K], box 128 x 64 rows, 128B swizzle
   CUtensorMap tmap_x;                 // bf16/f16 [M, K], box 64 x (tok / 2) rows, 128B swizzle
   const void* scales;                 // bf16 [N]
   void* y;

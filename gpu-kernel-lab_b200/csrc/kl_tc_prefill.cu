@@ -12,10 +12,12 @@
 //     192 columns) live in each CTA's TMEM for its 128 rows;
 //   * 4 epilogue warps per CTA apply the row scale (and SwiGLU), round to the
 //     activation type and store.
-// Per SM and K block this moves 8 KB of weights and 12 KB of tokens into
-// shared memory for 3.1 MFLOP, against 16 KB + 16 KB per 2.1 MFLOP for a
-// single-CTA 128 x 128 tile: the pair halves both the shared-memory traffic
-// and the conversion work per FLOP.
+// Per SM and 64-wide K step this moves 8 KB of weights and 12 KB of tokens
+// into shared memory for 3.1 MFLOP, against 16 KB + 16 KB per 2.1 MFLOP for
+// a single-CTA 128 x 128 tile: the pair halves both the shared-memory traffic
+// and the conversion work per FLOP.  A pipeline stage is 128 wide in K (two
+// such steps): the per-stage barrier round trips between converters, MMA and
+// TMA are paid once per 6.3 MFLOP per SM.
 //
 // Warp roles (15 warps per CTA): 0 weight TMA, 1 token TMA, 2 TMEM owner and
 // (leader) MMA issuer, 3-10 converters (two per TMEM lane quadrant, each one
@@ -32,17 +34,24 @@
 namespace kl {
 namespace {
 
-constexpr int kPfKb = 64;                        // K elements per stage
+constexpr int kPfKb = 128;                       // K elements per stage
+constexpr int kPfKAlign = 64;                    // K granularity the kernel takes (a last half stage is zero-filled)
+constexpr int kPfXAtomK = 64;                    // K elements of one 128-byte token row (bf16)
 constexpr int kPfRows = 128;                     // weight rows per CTA
 constexpr int kPfMaxTokens = 192;                // tokens per tile (MMA N): 192, 128 or 64
-constexpr int kPfW = 8;                          // weight stages
-constexpr int kPfX = 8;                          // token stages
-constexpr int kPfA = 4;                          // TMEM A stages
-constexpr int kPfWStage = kPfRows * kPfKb;       // 8 KB of int8
+constexpr int kPfW = 6;                          // weight stages (16 KB each)
+constexpr int kPfX = 4;                          // token stages (two 64-wide atoms each)
+constexpr int kPfAMax = 4;                       // TMEM A stages (at most)
+constexpr int kPfWStage = kPfRows * kPfKb;       // 16 KB of int8
 // token stage of one CTA: half the tile's tokens x 64 bf16 (12 KB at 192 tokens)
-__host__ __device__ constexpr int pf_xstage(int tok) { return (tok / 2) * kPfKb * 2; }
+__host__ __device__ constexpr int pf_xatom(int tok) { return (tok / 2) * kPfXAtomK * 2; }
+__host__ __device__ constexpr int pf_xstage(int tok) { return (kPfKb / kPfXAtomK) * pf_xatom(tok); }
 constexpr int kPfACols = kPfKb / 2;              // TMEM columns per A stage
-constexpr int kPfDCol0 = kPfA * kPfACols;        // 128
+// A stages fill the TMEM the two accumulator buffers leave: 2 at 192-token
+// tiles (the same K depth as 4 stages of 64), 4 at 128 or 64
+__host__ __device__ constexpr int pf_a_stages(int tok) {
+  return (512 - 2 * tok) / kPfACols < kPfAMax ? (512 - 2 * tok) / kPfACols : kPfAMax;
+}
 constexpr int kPfConv = 8;
 constexpr int kPfEpi0 = 3 + kPfConv;
 constexpr int kPfThreads = (kPfEpi0 + 4) * 32;   // 480
@@ -50,7 +59,8 @@ constexpr int kPfChunk = 32;                     // tokens per epilogue step
 constexpr int kPfXchHalf = 64 * (kPfChunk / 2 + 1);  // one direction of the SwiGLU exchange (padded rows)
 constexpr int kPfXchFloats = 2 * kPfXchHalf;
 constexpr int kPfStageBytes = 32 * kPfChunk * 2; // per epilogue warp: 32 rows x 32 tokens, bf16
-static_assert(kPfDCol0 + 2 * kPfMaxTokens == 512, "TMEM budget");
+static_assert(pf_a_stages(kPfMaxTokens) >= 2 && pf_a_stages(kPfMaxTokens) * kPfACols + 2 * kPfMaxTokens <= 512,
+              "TMEM budget");
 
 struct PfLayout {
   uint32_t w, x, xch, stage, tcache, bars, misc, total;
@@ -64,7 +74,7 @@ constexpr PfLayout pf_layout(int tok) {
   l.tcache = l.stage + 4 * kPfStageBytes;        // grouped launches: each problem's first tile
   l.bars = l.tcache + 4 * kMaxGroup;
   // w_full, w_empty [W]; x_full, x_empty [X]; a_full, a_empty [A]; d_full, d_empty [2]; done
-  l.misc = l.bars + 8 * (2 * kPfW + 2 * kPfX + 2 * kPfA + 5);
+  l.misc = l.bars + 8 * (2 * kPfW + 2 * kPfX + 2 * pf_a_stages(tok) + 5);
   l.total = l.misc + 16 + 1024;
   return l;
 }
@@ -157,6 +167,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   constexpr int kPfTokens = TOK;                 // tokens per tile (MMA N)
   constexpr int kPfHalf = TOK / 2;               // tokens per CTA
   constexpr int kPfXStage = pf_xstage(TOK);
+  constexpr int kPfXAtom = pf_xatom(TOK);
+  constexpr int kPfA = pf_a_stages(TOK);         // TMEM A stages
+  constexpr int kPfDCol0 = kPfA * kPfACols;      // accumulators after the A stages
+  static_assert(kPfXAtom % 1024 == 0, "token atoms stay 1024-byte aligned for the 128-byte swizzle");
   static_assert(TOK % kPfChunk == 0 && TOK <= kPfMaxTokens, "token tile");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -250,7 +264,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
         for (int kb = 0; kb < kbs; ++kb) {
           if (!pf_wait(x_empty(px.idx), px.phase ^ 1u, status)) { it = my_tiles; break; }
           if (leader) mbar_arrive_expect_tx(x_full(px.idx), 2 * kPfXStage);
-          tma_load_2d_pair(s_x + px.idx * kPfXStage, &p.tmap_x, kb * kPfKb, row, lead_full0 + 8u * px.idx);
+#pragma unroll
+          for (int a = 0; a < kPfKb / kPfXAtomK; ++a)
+            tma_load_2d_pair(s_x + px.idx * kPfXStage + a * kPfXAtom, &p.tmap_x, kb * kPfKb + a * kPfXAtomK, row,
+                             lead_full0 + 8u * px.idx);
           px.next();
         }
       }
@@ -278,7 +295,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
           if (elect_one()) {
 #pragma unroll
             for (int j = 0; j < kPfKb / 16; ++j)
-              tc_mma_pair_ts(d_tmem, a_tmem + 8u * j, xd + 2u * j, idesc, (kb == 0 && j == 0) ? 0u : 1u);
+              tc_mma_pair_ts(d_tmem, a_tmem + 8u * j,
+                             xd + static_cast<uint32_t>(((j >> 2) * kPfXAtom + (j & 3) * 32) >> 4), idesc,
+                             (kb == 0 && j == 0) ? 0u : 1u);
             tc_commit_pair_mc(x_empty(px.idx), 0x3);
             tc_commit_pair_mc(a_empty(pa.idx), 0x3);
             if (kb == kbs - 1) tc_commit_pair_mc(d_full(pd.idx), 0x3);
@@ -295,7 +314,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
   } else if (warp < kPfEpi0) {
     // ----------------------------------------------------------- converters
     const int q = warp & 3;
-    const int h = (warp - 3) >> 2;             // which 32-wide half of the K block
+    const int h = (warp - 3) >> 2;             // which 64-wide half of the K block
     const int r = q * 32 + lane;               // weight row of this CTA's 128
     const uint32_t lead_a_full0 = mapa_shared(a_full(0), 0);
     PfPipe pw{0, kPfW, 0}, pa{0, kPfA, 0};
@@ -309,19 +328,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) tc_prefill_kernel(const __grid_
         if (!(ok = pf_wait(a_empty(pa.idx), pa.phase ^ 1u, status))) break;
         tc_fence_after();
         const uint8_t* ws = smem + L.w + pw.idx * kPfWStage;
-        uint32_t part[16];
+        uint4 vv[4];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int g = 2 * h + c;             // 16-byte chunk of the 64-byte row (64B swizzle)
-          const uint4 v = *reinterpret_cast<const uint4*>(ws + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
-          const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int t4 = 0; t4 < 4; ++t4) {
-            if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
-            else s8x4_to_f16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
-          }
+        for (int c = 0; c < 4; ++c) {
+          const int g = 4 * h + c;             // 16-byte chunk of the 128-byte row (128B swizzle)
+          vv[c] = *reinterpret_cast<const uint4*>(ws + r * 128 + ((g ^ (r & 7)) << 4));
         }
-        tmem_st16(tmem + (static_cast<uint32_t>(q * 32) << 16) + pa.idx * kPfACols + 16u * h, part);
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t part[16];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint4 v = vv[2 * c2 + c];
+            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+              if constexpr (XBF16) s8x4_to_bf16x4_fma(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
+              else s8x4_to_f16x4(wd[t4], part[c * 8 + 2 * t4], part[c * 8 + 2 * t4 + 1]);
+            }
+          }
+          tmem_st16(tmem + (static_cast<uint32_t>(q * 32) << 16) + pa.idx * kPfACols + 32u * h + 16u * c2, part);
+        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -470,7 +497,7 @@ cudaError_t launch_pf(const PfLaunch& p, int grid, bool pdl, cudaStream_t s) {
 
 int prefill_threads() { return kPfThreads; }
 int prefill_smem_bytes(int tok) { return static_cast<int>(pf_layout(tok).total); }
-int prefill_k_block() { return kPfKb; }
+int prefill_k_block() { return kPfKAlign; }
 
 // Tokens per tile: the tile count of each choice is spread over the CTA pairs
 // in waves; a tile costs about (tile tokens + 48) token-steps of MMA and
@@ -498,7 +525,7 @@ void prefill_tiles(PfParams& p, bool swiglu, int sm_count) {
   p.n_tiles = swiglu ? (p.n_out + 127) / 128 : (p.n + 255) / 256;
   p.tok = prefill_choose_tokens(p.m, p.n_tiles, sm_count);
   p.m_tiles = (p.m + p.tok - 1) / p.tok;
-  p.kb_total = p.k / kPfKb;
+  p.kb_total = (p.k + kPfKb - 1) / kPfKb;
 }
 
 int prefill_grid(const PfParams& p, int sm_count) {
@@ -546,7 +573,7 @@ int prefill_group_tiles(PfParams* probs, int count, bool swiglu, int sm_count) {
     long long work = 0;                  // tile x K-block units
     for (int i = 0; i < count; ++i) {
       const int n_tiles = swiglu ? (probs[i].n_out + 127) / 128 : (probs[i].n + 255) / 256;
-      work += static_cast<long long>(n_tiles) * ((probs[i].m + tok - 1) / tok) * (probs[i].k / kPfKb);
+      work += static_cast<long long>(n_tiles) * ((probs[i].m + tok - 1) / tok) * ((probs[i].k + kPfKb - 1) / kPfKb);
     }
     const long long cost = ((work + pairs - 1) / pairs) * std::max(tok + 48, 192);
     if (best_cost < 0 || cost < best_cost) {
@@ -560,7 +587,7 @@ int prefill_group_tiles(PfParams* probs, int count, bool swiglu, int sm_count) {
     p.n_tiles = swiglu ? (p.n_out + 127) / 128 : (p.n + 255) / 256;
     p.tok = best;
     p.m_tiles = (p.m + best - 1) / best;
-    p.kb_total = p.k / kPfKb;
+    p.kb_total = (p.k + kPfKb - 1) / kPfKb;
     p.tile_begin = tiles;
     tiles += p.n_tiles * p.m_tiles;
   }
