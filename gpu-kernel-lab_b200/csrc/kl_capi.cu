@@ -962,7 +962,7 @@ int kl_describe_plan(int m, int n, int k, int w_format, int swiglu, int flags, i
     out[2] = prefill_threads();
     out[3] = prefill_smem_bytes(pf.tok);
     out[4] = pf.tok;                    // tokens per tile (pair MMA N)
-    out[5] = 8;                         // weight stages
+    out[5] = prefill_w_stages();        // weight stages
     out[6] = pf.n_tiles * pf.m_tiles;
     out[7] = pf.n_tiles * pf.m_tiles * pf.kb_total;
     if (out[1] % 2 || out[1] > (sm_count & ~1) || out[3] > 227 * 1024)

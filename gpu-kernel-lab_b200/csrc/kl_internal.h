@@ -206,6 +206,7 @@ struct PfLaunch {
   int* status;
 };
 int prefill_threads();
+int prefill_w_stages();               // weight-ring depth of the pair kernel
 int prefill_smem_bytes(int tok);
 int prefill_k_block();
 int prefill_choose_tokens(int m, int n_tiles, int sm_count);

@@ -498,6 +498,7 @@ cudaError_t launch_pf(const PfLaunch& p, int grid, bool pdl, cudaStream_t s) {
 int prefill_threads() { return kPfThreads; }
 int prefill_smem_bytes(int tok) { return static_cast<int>(pf_layout(tok).total); }
 int prefill_k_block() { return kPfKAlign; }
+int prefill_w_stages() { return kPfW; }
 
 // Tokens per tile: the tile count of each choice is spread over the CTA pairs
 // in waves; a tile costs about (tile tokens + 48) token-steps of MMA and
